@@ -1,0 +1,445 @@
+#!/usr/bin/env python3
+"""Decode-step KV-cache benchmark (paged append + per-layer paged gather).
+
+Workload: Llama-3.1-8B KV shape -- 32 layers, 8 KV heads, head_dim 128,
+block 16, bf16; batch 64, context lengths uniform in [512, 4096]; every step
+appends one token per sequence to every layer, then gathers every layer's
+K/V for all sequences through the block tables.  Block tables are drawn
+from a seeded permutation of a pool sized 1.25x the blocks in use.
+
+With N GPUs (one process per GPU under torchrun) the 8 KV heads are split
+over the GPUs: each rank owns 8/N heads of every block and runs the same
+step on them; there is no collective in the step.
+
+Metric: algorithmic HBM GB/s of the step (K/V bytes read + written by the
+append and the gathers), whole job; also microseconds per decode step.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+"""
+import argparse
+import json
+import os
+import shutil
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "rmlx-serve_b200"))
+
+LAYERS, HEADS, HEAD_DIM, BLOCK, BATCH = 32, 8, 128, 16, 64
+CTX_LO, CTX_HI = 512, 4096
+ESIZE = 2  # bf16
+SEED = 0x5EED + 2
+METRIC = "KV append+gather HBM GB/s (decode step, Llama-3.1-8B KV shape)"
+WORKLOAD = ("decode-step KV ops: 32 layers x 8 KV heads x 128, block 16, bf16, batch 64, "
+            "ctx U[512,4096], append 1 token/seq/layer then paged gather of every layer")
+
+
+def env_int(name, default):
+    try:
+        return int(os.environ.get(name, default))
+    except ValueError:
+        return default
+
+
+def measured_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def profile_traffic(name):
+    """Per-launch DRAM bytes of `name` from its committed ncu summary, if any."""
+    p = os.path.join(ROOT, "profiles", name)
+    try:
+        for line in open(p):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":")[1])
+    except OSError:
+        pass
+    return None
+
+
+def make_workload(steps_total, heads_local):
+    """Seeded lengths, block tables (through the product's block manager) and
+    per-step slot mappings for `steps_total` decode steps."""
+    import rmlx_kv
+    rng = np.random.default_rng(SEED)
+    lens0 = rng.integers(CTX_LO, CTX_HI + 1, size=BATCH).astype(np.int64)
+    final = lens0 + steps_total
+    need = (final + BLOCK - 1) // BLOCK
+    num_blocks = int(np.ceil(1.25 * need.sum()))
+    mgr = rmlx_kv.PagedCacheManager(BLOCK, num_blocks)
+    # Make the free list a seeded permutation of the pool: allocate all, free
+    # in permuted order (FIFO reuse hands them out in that order).
+    allb = mgr.allocate_n(num_blocks)
+    mgr.free_n(rng.permutation(allb))
+    width = int(need.max())
+    bt = np.zeros((BATCH, width), dtype=np.int32)
+    nblk = np.zeros(BATCH, dtype=np.int64)
+    for s in range(BATCH):
+        n0 = (int(lens0[s]) + BLOCK - 1) // BLOCK
+        bt[s, :n0] = mgr.allocate_n(n0)
+        nblk[s] = n0
+    slots = np.zeros((steps_total, BATCH), dtype=np.int32)
+    for st in range(steps_total):
+        for s in range(BATCH):
+            p = int(lens0[s]) + st
+            while p // BLOCK >= nblk[s]:
+                bt[s, nblk[s]] = mgr.allocate_n(1)[0]
+                nblk[s] += 1
+            slots[st, s] = bt[s, p // BLOCK] * BLOCK + p % BLOCK
+    return dict(lens0=lens0, bt=bt, slots=slots, num_blocks=num_blocks, mgr=mgr, rng=rng)
+
+
+def step_bytes(lens, heads):
+    """Algorithmic bytes of one step: append (read new rows + write them) and
+    a gather of every layer (read rows + write rows, K and V), plus the
+    block-table entries and lengths the gathers read."""
+    row = heads * HEAD_DIM * ESIZE
+    append = 2 * 2 * BATCH * LAYERS * row
+    blocks = int(((lens + BLOCK - 1) // BLOCK).sum())
+    gather_one = 2 * 2 * int(lens.sum()) * row + 4 * blocks + 4 * BATCH
+    return append, gather_one
+
+
+class DevView:
+    """Zero-copy torch view of raw device memory (for filling the pool)."""
+
+    def __init__(self, ptr, nbytes):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False),
+                                         "version": 3}
+
+
+class Clocks:
+    """nvidia-smi sampling of SM clocks and throttle reasons during timing."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        if not shutil.which("nvidia-smi"):
+            return
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        self.f = open(self.path, "w")
+        self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.Q}",
+                                      "--format=csv,noheader,nounits", "-lms", "100"], stdout=self.f,
+                                     stderr=subprocess.DEVNULL)
+        time.sleep(0.3)
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.f.close()
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in open(self.path):
+            p = [x.strip() for x in ln.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                sm.append(float(p[1]))
+                mx = max(mx, float(p[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, p[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        os.unlink(self.path)
+        if not sm:
+            return None
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_sample(steps, warm, threads, lens0, bt, slots, num_blocks):
+    """The oracle (CPU restatement of the reference's row copies) on the host
+    cores: one layer of every step -- append 1 token per sequence, then the
+    full gather of that layer.  Returns (GB/s, seconds per sampled step)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as orc
+    g = orc.Geo(1, HEADS, HEAD_DIM, BLOCK, num_blocks, ESIZE)
+    pool = np.zeros(g.pool_bytes(), dtype=np.uint8)
+    rng = np.random.default_rng(SEED + 1)
+    pool[:] = rng.integers(0, 256, size=pool.size, dtype=np.uint8)
+    lens_max = lens0 + slots.shape[0]
+    tot = int(lens_max.sum()) * HEADS * HEAD_DIM
+    ok = np.empty(tot, dtype=np.uint16)
+    ov = np.empty(tot, dtype=np.uint16)
+    kin = orc.f32_to_dtype(rng.standard_normal((BATCH, HEADS, HEAD_DIM), dtype=np.float32), orc.BF16)
+    total_bytes, t_total = 0, 0.0
+    for st in range(warm + steps):
+        lens = (lens0 + st + 1).astype(np.int32)
+        t0 = time.perf_counter()
+        orc.paged_append(pool, g, 0, 1, kin, kin, 0, HEADS * HEAD_DIM, HEAD_DIM, slots[st].astype(np.int64))
+        orc.paged_gather(pool, g, 0, bt, bt.shape[1], lens, ok, ov, threads=threads)
+        dt = time.perf_counter() - t0
+        if st >= warm:
+            a, gth = step_bytes(lens.astype(np.int64), HEADS)
+            total_bytes += a / LAYERS + gth
+            t_total += dt
+    return total_bytes / t_total / 1e9, t_total / steps
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference's CPU path (the oracle port; the Rust
+    reference cannot be built in this image) on all host cores."""
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    steps, warm = max(args.steps // 5, 2), min(args.warmup, 2)
+    w = make_workload(warm + steps, HEADS)
+    gbs, sec = cpu_sample(steps, warm, threads, w["lens0"], w["bt"], w["slots"], w["num_blocks"])
+    ms_full = sec * LAYERS * 1e3  # one sampled layer per step -> a full 32-layer step
+    sample = (f"1 of 32 layers per step (append 1 token/seq + full gather of that layer), batch 64, "
+              f"{steps} timed steps after {warm} warm-up; GB/s is per sampled byte, ms_per_step scaled x32")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 2), "unit": "GB/s", "n_gpus": world,
+        "steps": steps, "warmup": warm, "ms_per_step": round(ms_full, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "batch": BATCH, "layers": LAYERS, "kv_heads": HEADS,
+                   "head_dim": HEAD_DIM, "block_size": BLOCK},
+        "cpu_baseline": {"value": round(gbs, 2), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    rank, world, local = env_int("RANK", 0), env_int("WORLD_SIZE", 1), env_int("LOCAL_RANK", 0)
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+
+    import torch
+    import rmlx_kv
+    from rmlx_kv import _lib
+
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    dev = torch.cuda.current_device()
+    if HEADS % world:
+        raise SystemExit(f"{HEADS} KV heads do not split over {world} GPUs")
+    H = HEADS // world
+    W, K = args.warmup, args.steps
+    wl = make_workload(W + K, H)
+    lens0, bt, slots, num_blocks = wl["lens0"], wl["bt"], wl["slots"], wl["num_blocks"]
+
+    pool = rmlx_kv.KVPool(LAYERS, H, HEAD_DIM, BLOCK, num_blocks, dtype=rmlx_kv.BF16, head_offset=rank * H,
+                          device=dev)
+    # K/V ~ N(0,1): fill every block of the pool on the device.
+    gen = torch.Generator(device="cuda").manual_seed(SEED + rank)
+    view = torch.as_tensor(DevView(pool.layout.base, pool.layout.bytes), device="cuda").view(torch.bfloat16)
+    chunk = 1 << 28
+    for o in range(0, view.numel(), chunk):
+        n = min(chunk, view.numel() - o)
+        view[o:o + n].normal_(generator=gen)
+    del view
+
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+    kv_shape = (W + K, LAYERS, BATCH, H, HEAD_DIM)
+    new_k = torch.randn(kv_shape, device="cuda", dtype=torch.bfloat16, generator=gen)
+    new_v = torch.randn(kv_shape, device="cuda", dtype=torch.bfloat16, generator=gen)
+    slots_d = torch.from_numpy(slots).cuda()
+    bt_d = torch.from_numpy(bt).cuda()
+    lens_steps = np.stack([(lens0 + s + 1).astype(np.int32) for s in range(W + K)])
+    lens_d = torch.from_numpy(lens_steps).cuda()
+    max_tok = int(lens_steps[-1].sum())
+    out_k = torch.empty(max_tok * H * HEAD_DIM, device="cuda", dtype=torch.bfloat16)
+    out_v = torch.empty_like(out_k)
+    ts, ls = H * HEAD_DIM, BATCH * H * HEAD_DIM
+    h = pool.handle
+    lib = _lib.lib
+
+    def launch_step(s, ev_pairs=None):
+        rc = lib.rmlx_kv_append(h, 0, LAYERS, new_k[s].data_ptr(), new_v[s].data_ptr(), ls, ts, HEAD_DIM,
+                                slots_d[s].data_ptr(), BATCH, sp)
+        for layer in range(LAYERS):
+            if ev_pairs is not None:
+                ev_pairs[layer][0].record(stream)
+            rc |= lib.rmlx_kv_gather(h, layer, bt_d.data_ptr(), bt.shape[1], lens_d[s].data_ptr(), BATCH,
+                                     out_k.data_ptr(), out_v.data_ptr(), sp)
+            if ev_pairs is not None:
+                ev_pairs[layer][1].record(stream)
+        return rc
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    rc = 0
+    for s in range(W):
+        rc |= launch_step(s)
+    if rc or pool.check() != 0:
+        raise SystemExit("device-side validation error during warm-up")
+
+    clocks = Clocks(dev)
+    clocks.start()
+    ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(LAYERS)]
+          for _ in range(K)]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for i in range(K):
+        rc |= launch_step(W + i, ev[i])
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    elapsed_ms = max_over_ranks(e0.elapsed_time(e1))
+    gather_ms = [ev[i][l][0].elapsed_time(ev[i][l][1]) for i in range(K) for l in range(LAYERS)]
+    if rc or pool.check() != 0:
+        raise SystemExit("launch or device-side validation error in the timed region")
+
+    # Algorithmic bytes over the timed steps, all ranks.
+    tot_bytes, gather_bytes = 0, []
+    for i in range(K):
+        a, g1 = step_bytes(lens_steps[W + i].astype(np.int64), H)
+        tot_bytes += a + LAYERS * g1
+        gather_bytes += [g1] * LAYERS
+    tot_bytes *= world
+    value = tot_bytes / (elapsed_ms * 1e-3) / 1e9
+    ms_per_step = elapsed_ms / K
+
+    # ---- e2e: the same steps through the public API with host buffers ----
+    # Per step: block-manager allocation for sequences crossing a block
+    # boundary, H2D of the new K/V (pinned), slots, block tables and lengths,
+    # the append and 32 gathers, and a D2H read of the step's status word.
+    mgr = rmlx_kv.PagedCacheManager(BLOCK, num_blocks)
+    rng = np.random.default_rng(SEED + 7)
+    mgr.free_n(rng.permutation(mgr.allocate_n(num_blocks)))
+    host_bt = np.zeros_like(bt)
+    nblk = np.zeros(BATCH, dtype=np.int64)
+    for s in range(BATCH):
+        n0 = (int(lens0[s]) + BLOCK - 1) // BLOCK
+        host_bt[s, :n0] = mgr.allocate_n(n0)
+        nblk[s] = n0
+    pin_k = torch.empty((K, LAYERS, BATCH, H, HEAD_DIM), dtype=torch.bfloat16, pin_memory=True)
+    pin_v = torch.empty_like(pin_k, pin_memory=True)
+    pin_k.copy_(new_k[W:W + K].cpu())
+    pin_v.copy_(new_v[W:W + K].cpu())
+    pin_bt = torch.from_numpy(host_bt).pin_memory()
+    pin_slots = torch.empty(BATCH, dtype=torch.int32, pin_memory=True)
+    pin_lens = torch.empty(BATCH, dtype=torch.int32, pin_memory=True)
+    dk = torch.empty((LAYERS, BATCH, H, HEAD_DIM), device="cuda", dtype=torch.bfloat16)
+    dv = torch.empty_like(dk)
+    d_slots = torch.empty(BATCH, dtype=torch.int32, device="cuda")
+    d_lens = torch.empty(BATCH, dtype=torch.int32, device="cuda")
+    d_bt = torch.empty_like(bt_d)
+    err_word = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+    h2d = 2 * dk.numel() * ESIZE + 2 * BATCH * 4 + host_bt.nbytes
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(K):
+        lens_np = pin_lens.numpy()
+        sl = pin_slots.numpy()
+        btn = pin_bt.numpy()
+        for s in range(BATCH):
+            p = int(lens0[s]) + W + i  # position written this step
+            while p // BLOCK >= nblk[s]:
+                btn[s, nblk[s]] = mgr.allocate_n(1)[0]
+                nblk[s] += 1
+            sl[s] = btn[s, p // BLOCK] * BLOCK + p % BLOCK
+            lens_np[s] = p + 1
+        dk.copy_(pin_k[i], non_blocking=True)
+        dv.copy_(pin_v[i], non_blocking=True)
+        d_slots.copy_(pin_slots, non_blocking=True)
+        d_lens.copy_(pin_lens, non_blocking=True)
+        d_bt.copy_(pin_bt, non_blocking=True)
+        rc |= lib.rmlx_kv_append(h, 0, LAYERS, dk.data_ptr(), dv.data_ptr(), ls, ts, HEAD_DIM,
+                                 d_slots.data_ptr(), BATCH, sp)
+        for layer in range(LAYERS):
+            rc |= lib.rmlx_kv_gather(h, layer, d_bt.data_ptr(), bt.shape[1], d_lens.data_ptr(), BATCH,
+                                     out_k.data_ptr(), out_v.data_ptr(), sp)
+        err_word[0] = pool.check()  # the step's status word, read back to the host
+        if rc or err_word[0]:
+            raise SystemExit("launch or device-side validation error in the e2e loop")
+    torch.cuda.synchronize()
+    barrier()
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    clk = clocks.stop()
+    e2e_value = tot_bytes / e2e_s / 1e9
+
+    peak, peak_kind = measured_peak()
+    g_bytes = float(np.mean(gather_bytes))
+    g_ms = float(np.mean(gather_ms))
+    achieved = g_bytes / (g_ms * 1e-3) / 1e9
+    traffic = profile_traffic("gather_rows_kernel_llama8b_decode.txt")
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        gbs, _ = cpu_sample(8, 1, threads, lens0, bt[:, :], slots, num_blocks)
+        cpu = {"value": round(gbs, 2), "unit": "GB/s", "cores": threads, "kind": "port",
+               "sample": "oracle row-copy append+gather, 1 of 32 layers per step, batch 64, 8 timed steps"}
+
+    if rank == 0:
+        out = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": K,
+            "warmup": W, "ms_per_step": round(ms_per_step, 4), "us_per_step": round(ms_per_step * 1e3, 1),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": WORKLOAD, "batch": BATCH, "layers": LAYERS, "kv_heads": HEADS,
+                       "kv_heads_per_gpu": H, "head_dim": HEAD_DIM, "block_size": BLOCK,
+                       "pool_blocks": num_blocks, "sharding": f"kv-head x{world}",
+                       "l2": "inputs larger than L2: each gather launch moves ~1.2 GB/N, no flush"},
+            "roofline": {"bound": "hbm", "kernel": "gather_rows_kernel", "achieved": round(achieved, 1),
+                         "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "frac_of_8000_nominal": round(achieved / 8000.0, 4), "traffic": traffic,
+                         "algorithmic_bytes_per_launch": int(g_bytes), "launch_ms": round(g_ms, 4)},
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
+                    "d2h_bytes_per_step": 4, "ms_per_step": round(e2e_s / K * 1e3, 4)},
+            "gpu_launches": K * (1 + LAYERS),
+            "cpu_baseline": cpu,
+            "clocks": clk,
+        }
+        print(json.dumps(out), flush=True)
+    pool.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,319 @@
+/*
+ * rmlx_kv.h -- C ABI of the B200 paged KV-cache store.
+ *
+ * Drop-in for the KV-cache crate of rmlx-serve (crates/rmlx-serve-cache).
+ * The reference is a Rust crate with no FFI of its own; every entry point
+ * below replaces one public item of that crate (cited as file:line relative
+ * to the crate's src/ directory) or is a device operation the crate's types
+ * describe but leave to an external GPU library (cited likewise).
+ *
+ * Conventions
+ *   - Every call returns rmlx_status (0 = RMLX_OK).  Where the reference
+ *     panics (assert!), the call returns the matching error code and leaves
+ *     the state untouched.  Where it returns Option::None, the call returns
+ *     RMLX_OK with *found (or *copied) = 0.
+ *   - Block ids are int32_t (the reference uses usize); tokens are uint32_t;
+ *     hashes are uint64_t; counts are size_t.
+ *   - Handles are not thread-safe; the caller serialises calls on one handle,
+ *     as the reference's &mut self methods require.
+ *   - Device entry points take device pointers and a stream (a cudaStream_t
+ *     passed as void*, NULL = the legacy default stream); they enqueue work
+ *     and return without synchronising.  Device-side validation failures (a
+ *     block id or slot outside the pool) skip the offending row and latch an
+ *     error word that rmlx_kv_pool_check() reads back.
+ *   - rmlx_last_error() returns a thread-local message for the last failure.
+ */
+#ifndef RMLX_KV_H
+#define RMLX_KV_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define RMLX_API __attribute__((visibility("default")))
+#else
+#define RMLX_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum rmlx_status {
+  RMLX_OK = 0,
+  RMLX_E_RANGE = 1,       /* block id out of range   (paged_cache.rs:126-130) */
+  RMLX_E_DOUBLE_FREE = 2, /* free of a free block    (paged_cache.rs:132-135) */
+  RMLX_E_OVERFLOW = 3,    /* append past block_size  (paged_cache.rs:290-296) */
+  RMLX_E_FREE_BLOCK = 4,  /* share a free block      (paged_cache.rs:177-180) */
+  RMLX_E_BAD_ARG = 5,     /* bits/length/layout misuse (quantized_cache.rs:57-60,97-108) */
+  RMLX_E_EXHAUSTED = 6,   /* device memory or capacity exhausted */
+  RMLX_E_CUDA = 7,        /* a CUDA runtime call failed */
+  RMLX_E_NCCL = 8,        /* an NCCL call failed */
+  RMLX_E_TIMEOUT = 9,     /* a bounded wait ran out */
+  RMLX_E_DEVICE = 10      /* a kernel flagged an out-of-pool block id or slot */
+} rmlx_status;
+
+typedef enum rmlx_dtype { RMLX_F32 = 0, RMLX_F16 = 1, RMLX_BF16 = 2 } rmlx_dtype;
+
+RMLX_API const char* rmlx_status_string(rmlx_status s);
+RMLX_API const char* rmlx_last_error(void);
+/* Library version, e.g. "0.1.0". */
+RMLX_API const char* rmlx_version(void);
+
+/* ======================================================================
+ * PagedCacheManager -- paged_cache.rs:71-302 (block allocator, refcounts,
+ * copy-on-write metadata, content-hash index).  Host-side metadata.
+ * ==================================================================== */
+typedef struct rmlx_block_manager rmlx_block_manager;
+
+/* KVCacheBlock view -- paged_cache.rs:14-26 */
+typedef struct rmlx_block_view {
+  int32_t block_id;
+  size_t ref_count;
+  int32_t has_hash; /* hash: Option<u64> */
+  uint64_t hash;
+  size_t num_filled;
+} rmlx_block_view;
+
+/* PagedCacheManager::new -- paged_cache.rs:90-104 */
+RMLX_API rmlx_status rmlx_block_manager_new(size_t block_size, size_t num_blocks, rmlx_block_manager** out);
+RMLX_API void rmlx_block_manager_destroy(rmlx_block_manager* m);
+/* allocate -- paged_cache.rs:110-115.  *found = 0 when the pool is empty. */
+RMLX_API rmlx_status rmlx_block_manager_allocate(rmlx_block_manager* m, int32_t* block_id, int32_t* found);
+/* Batched allocate (n calls of allocate in order); *n_got < n when exhausted. */
+RMLX_API rmlx_status rmlx_block_manager_allocate_n(rmlx_block_manager* m, size_t n, int32_t* block_ids, size_t* n_got);
+/* free -- paged_cache.rs:125-149 */
+RMLX_API rmlx_status rmlx_block_manager_free(rmlx_block_manager* m, int32_t block_id);
+/* Batched free (n calls of free in order; stops at the first error). */
+RMLX_API rmlx_status rmlx_block_manager_free_n(rmlx_block_manager* m, const int32_t* block_ids, size_t n);
+/* ref_count -- paged_cache.rs:157-163 */
+RMLX_API rmlx_status rmlx_block_manager_ref_count(const rmlx_block_manager* m, int32_t block_id, size_t* out);
+/* increment_ref -- paged_cache.rs:172-182 */
+RMLX_API rmlx_status rmlx_block_manager_increment_ref(rmlx_block_manager* m, int32_t block_id);
+/* copy_on_write -- paged_cache.rs:197-224.  *copied = 0 for None (unshared
+ * block, or no free block); the KV bytes are moved by rmlx_kv_copy_blocks. */
+RMLX_API rmlx_status rmlx_block_manager_copy_on_write(rmlx_block_manager* m, int32_t block_id, int32_t* new_id,
+                                             int32_t* copied);
+/* num_free_blocks / num_allocated_blocks / num_blocks / block_size --
+ * paged_cache.rs:227-244 */
+RMLX_API size_t rmlx_block_manager_num_free_blocks(const rmlx_block_manager* m);
+RMLX_API size_t rmlx_block_manager_num_allocated_blocks(const rmlx_block_manager* m);
+RMLX_API size_t rmlx_block_manager_num_blocks(const rmlx_block_manager* m);
+RMLX_API size_t rmlx_block_manager_block_size(const rmlx_block_manager* m);
+/* get_block -- paged_cache.rs:249-251.  *found = 0 when out of range.  Up to
+ * `cap` token ids are copied to `tokens` (may be NULL when cap = 0). */
+RMLX_API rmlx_status rmlx_block_manager_get_block(const rmlx_block_manager* m, int32_t block_id, rmlx_block_view* view,
+                                         uint32_t* tokens, size_t cap, int32_t* found);
+/* register_hash -- paged_cache.rs:265-272 */
+RMLX_API rmlx_status rmlx_block_manager_register_hash(rmlx_block_manager* m, int32_t block_id, uint64_t hash);
+/* lookup_hash -- paged_cache.rs:278-282 */
+RMLX_API rmlx_status rmlx_block_manager_lookup_hash(const rmlx_block_manager* m, uint64_t hash, int32_t* block_id,
+                                           int32_t* found);
+/* append_tokens -- paged_cache.rs:288-301 */
+RMLX_API rmlx_status rmlx_block_manager_append_tokens(rmlx_block_manager* m, int32_t block_id, const uint32_t* tokens,
+                                             size_t n);
+
+/* ======================================================================
+ * PrefixCacheManager -- prefix_cache.rs:44-292 (token trie + LRU).
+ * ==================================================================== */
+typedef struct rmlx_prefix_cache rmlx_prefix_cache;
+
+/* new -- prefix_cache.rs:66-77 */
+RMLX_API rmlx_status rmlx_prefix_cache_new(size_t max_blocks, rmlx_prefix_cache** out);
+RMLX_API void rmlx_prefix_cache_destroy(rmlx_prefix_cache* p);
+/* lookup -- prefix_cache.rs:85-113.  `block_ids` must hold n entries (a
+ * lookup matches at most one block per token); *n_out = matched blocks. */
+RMLX_API rmlx_status rmlx_prefix_cache_lookup(rmlx_prefix_cache* p, const uint32_t* tokens, size_t n, int32_t* block_ids,
+                                     size_t* n_out);
+/* insert -- prefix_cache.rs:126-179 */
+RMLX_API rmlx_status rmlx_prefix_cache_insert(rmlx_prefix_cache* p, const uint32_t* tokens, size_t n,
+                                     const int32_t* block_ids, size_t n_blocks);
+/* evict_lru -- prefix_cache.rs:187-232.  *found = 0 when nothing is cached. */
+RMLX_API rmlx_status rmlx_prefix_cache_evict_lru(rmlx_prefix_cache* p, int32_t* block_id, int32_t* found);
+/* hit_rate / num_blocks / max_blocks / is_full / num_nodes --
+ * prefix_cache.rs:266-291 */
+RMLX_API double rmlx_prefix_cache_hit_rate(const rmlx_prefix_cache* p);
+RMLX_API size_t rmlx_prefix_cache_num_blocks(const rmlx_prefix_cache* p);
+RMLX_API size_t rmlx_prefix_cache_max_blocks(const rmlx_prefix_cache* p);
+RMLX_API int32_t rmlx_prefix_cache_is_full(const rmlx_prefix_cache* p);
+RMLX_API size_t rmlx_prefix_cache_num_nodes(const rmlx_prefix_cache* p);
+
+/* ======================================================================
+ * MemoryAwarePrefixCache -- memory.rs:10-158.  available_memory_mb() is
+ * usize::MAX as on the reference's non-macOS build (memory.rs:88-91).
+ * ==================================================================== */
+typedef struct rmlx_mem_prefix_cache rmlx_mem_prefix_cache;
+
+/* new (bytes_per_block 4096) -- memory.rs:31-45 */
+RMLX_API rmlx_status rmlx_mem_prefix_cache_new(size_t max_blocks, size_t memory_limit_mb, rmlx_mem_prefix_cache** out);
+/* with_block_size -- memory.rs:53-64 */
+RMLX_API rmlx_status rmlx_mem_prefix_cache_with_block_size(size_t max_blocks, size_t memory_limit_mb,
+                                                  size_t bytes_per_block, rmlx_mem_prefix_cache** out);
+RMLX_API void rmlx_mem_prefix_cache_destroy(rmlx_mem_prefix_cache* p);
+/* should_evict -- memory.rs:99-110 */
+RMLX_API int32_t rmlx_mem_prefix_cache_should_evict(const rmlx_mem_prefix_cache* p);
+/* evict_until_threshold -- memory.rs:117-136 */
+RMLX_API rmlx_status rmlx_mem_prefix_cache_evict_until_threshold(rmlx_mem_prefix_cache* p);
+/* lookup -- memory.rs:141-143 (same contract as rmlx_prefix_cache_lookup) */
+RMLX_API rmlx_status rmlx_mem_prefix_cache_lookup(rmlx_mem_prefix_cache* p, const uint32_t* tokens, size_t n,
+                                         int32_t* block_ids, size_t* n_out);
+/* insert -- memory.rs:149-158 */
+RMLX_API rmlx_status rmlx_mem_prefix_cache_insert(rmlx_mem_prefix_cache* p, const uint32_t* tokens, size_t n,
+                                         const int32_t* block_ids, size_t n_blocks);
+/* evict_lru -- memory.rs:161-168 */
+RMLX_API rmlx_status rmlx_mem_prefix_cache_evict_lru(rmlx_mem_prefix_cache* p, int32_t* block_id, int32_t* found);
+/* The reference drops the ids that insert()/evict_until_threshold() evict
+ * (memory.rs:121); this pops them, oldest first, so a caller can free the
+ * blocks.  *n_out = ids written (<= cap). */
+RMLX_API rmlx_status rmlx_mem_prefix_cache_drain_evicted(rmlx_mem_prefix_cache* p, int32_t* block_ids, size_t cap,
+                                                size_t* n_out);
+RMLX_API double rmlx_mem_prefix_cache_hit_rate(const rmlx_mem_prefix_cache* p);
+RMLX_API size_t rmlx_mem_prefix_cache_current_usage_bytes(const rmlx_mem_prefix_cache* p);
+RMLX_API size_t rmlx_mem_prefix_cache_memory_limit_bytes(const rmlx_mem_prefix_cache* p);
+RMLX_API size_t rmlx_mem_prefix_cache_num_blocks(const rmlx_mem_prefix_cache* p);
+
+/* ======================================================================
+ * QuantizedKVCache -- quantized_cache.rs:14-296.  Same host-slice API and
+ * byte layout as the reference (per layer, append-call order, groups of
+ * group_size over each appended [heads, tokens, head_dim] slice); storage
+ * lives in device memory and (de)quantisation runs on the GPU.  Calls are
+ * synchronous, like the reference.
+ * ==================================================================== */
+typedef struct rmlx_qcache rmlx_qcache;
+
+/* new -- quantized_cache.rs:50-81 (bits 4 or 8) */
+RMLX_API rmlx_status rmlx_qcache_new(size_t num_layers, size_t num_kv_heads, size_t head_dim, size_t bits,
+                            size_t group_size, int device, rmlx_qcache** out);
+RMLX_API void rmlx_qcache_destroy(rmlx_qcache* q);
+/* append -- quantized_cache.rs:89-127.  keys/values: host f32 slices of
+ * length `len` = num_kv_heads * new_tokens * head_dim. */
+RMLX_API rmlx_status rmlx_qcache_append(rmlx_qcache* q, size_t layer, const float* keys, const float* values, size_t len,
+                               size_t new_tokens);
+/* get_keys_dequantized / get_values_dequantized -- quantized_cache.rs:133-151.
+ * `out` holds `cap` floats; *n_out = values produced (call with out = NULL,
+ * cap = 0 to size the buffer). */
+RMLX_API rmlx_status rmlx_qcache_get_keys_dequantized(rmlx_qcache* q, size_t layer, float* out, size_t cap, size_t* n_out);
+RMLX_API rmlx_status rmlx_qcache_get_values_dequantized(rmlx_qcache* q, size_t layer, float* out, size_t cap,
+                                               size_t* n_out);
+/* seq_len / num_layers / bits / group_size -- quantized_cache.rs:154-171 */
+RMLX_API size_t rmlx_qcache_seq_len(const rmlx_qcache* q);
+RMLX_API size_t rmlx_qcache_num_layers(const rmlx_qcache* q);
+RMLX_API size_t rmlx_qcache_bits(const rmlx_qcache* q);
+RMLX_API size_t rmlx_qcache_group_size(const rmlx_qcache* q);
+/* Stored state of one layer (which = 0 keys, 1 values): packed bytes and the
+ * per-group f32 scales and zeros (quantized_cache.rs:16-26).  *n_bytes and
+ * *n_groups report the full sizes; up to the caps are copied. */
+RMLX_API rmlx_status rmlx_qcache_raw(rmlx_qcache* q, size_t layer, int32_t which, uint8_t* bytes, size_t bytes_cap,
+                            float* scales, float* zeros, size_t groups_cap, size_t* n_bytes, size_t* n_groups);
+
+/* ======================================================================
+ * Paged KV pool on one GPU (device data plane).
+ *
+ * The reference keeps KV bytes in rmlx_nn::LayerKvCache, an external GPU
+ * buffer per sequence (kv_cache.rs:16-54; appended and read inside the
+ * model forward, transformer.rs:125-129).  Its only in-crate value-moving
+ * append/gather is RotatingKVCache::append / get_logical_order
+ * (rotating_cache.rs:94-197).  The pool below stores those rows in the
+ * blocks that PagedCacheManager hands out.
+ *
+ * Layout (block-major): pool[block][layer][kv][head][slot][row].  One
+ * (block, layer, kv, head) tile is block_size rows of head_dim elements
+ * (plain pools) or block_size code rows followed by block_size meta rows of
+ * head_dim/group_size (scale, zero) pairs (quantised pools), padded to 16 B.
+ * A pool holds `num_kv_heads` heads: one KV-head shard of a model when the
+ * heads are split over GPUs.
+ * ==================================================================== */
+typedef struct rmlx_pool_config {
+  int32_t num_layers;
+  int32_t num_kv_heads; /* heads held by this pool (one shard) */
+  int32_t head_dim;
+  int32_t block_size;   /* tokens per block (CacheConfig default 16) */
+  int32_t num_blocks;
+  int32_t dtype;        /* rmlx_dtype of appended and gathered rows */
+  int32_t quant_bits;   /* 0 = plain, 8 or 4 = group-affine codes */
+  int32_t group_size;   /* quantisation group along head_dim (power of two) */
+  int32_t meta_dtype;   /* RMLX_F32 (reference-exact) or RMLX_F16 */
+  int32_t head_offset;  /* first global KV head of this shard */
+} rmlx_pool_config;
+
+typedef struct rmlx_pool_layout {
+  void* base;           /* device pointer of block 0 */
+  size_t bytes;         /* total pool bytes */
+  size_t tile_bytes;    /* bytes of one (block, layer, kv, head) tile */
+  size_t block_bytes;   /* bytes of one block across layers, kv, heads */
+  size_t row_bytes;     /* bytes of one stored row (codes for quantised pools) */
+  size_t meta_row_bytes;/* bytes of one meta row (0 for plain pools) */
+} rmlx_pool_layout;
+
+typedef struct rmlx_kv_pool rmlx_kv_pool;
+
+RMLX_API rmlx_status rmlx_kv_pool_new(const rmlx_pool_config* cfg, int device, rmlx_kv_pool** out);
+RMLX_API void rmlx_kv_pool_destroy(rmlx_kv_pool* p);
+RMLX_API rmlx_status rmlx_kv_pool_layout(const rmlx_kv_pool* p, rmlx_pool_layout* out);
+/* Reads and clears the device error word (synchronises the pool's device). */
+RMLX_API rmlx_status rmlx_kv_pool_check(rmlx_kv_pool* p, int32_t* device_error);
+
+/* Synchronous copies between host memory and pool bytes
+ * [offset, offset + nbytes) (e.g. to save or restore blocks, the role of
+ * save_prompt_cache / load_prompt_cache, prompt_cache.rs:63-210). */
+RMLX_API rmlx_status rmlx_kv_pool_read(rmlx_kv_pool* p, size_t offset, size_t nbytes, void* host_dst);
+RMLX_API rmlx_status rmlx_kv_pool_write(rmlx_kv_pool* p, size_t offset, size_t nbytes, const void* host_src);
+
+/* Append (reshape-and-cache) -- per-token row copy of
+ * RotatingKVCache::append (rotating_cache.rs:126-136) into paged slots.
+ * Writes the K and V rows of `num_tokens` tokens for layers
+ * [layer_begin, layer_begin + num_layers).  Row (l, t, h) of k/v starts at
+ * element (l - layer_begin) * layer_stride + t * token_stride + h * head_stride
+ * (element type = cfg.dtype; strides * element size must be multiples of
+ * 16 B).  slot_mapping[t] = block * block_size + offset; a negative slot
+ * skips the token.  A quantised pool quantises each row on the way in with
+ * the group math of quantize_group (quantized_cache.rs:232-273). */
+RMLX_API rmlx_status rmlx_kv_append(rmlx_kv_pool* p, int32_t layer_begin, int32_t num_layers, const void* k, const void* v,
+                           int64_t layer_stride, int64_t token_stride, int64_t head_stride,
+                           const int32_t* slot_mapping, int32_t num_tokens, void* stream);
+
+/* Gather -- RotatingKVCache::get_logical_order (rotating_cache.rs:162-197)
+ * over block tables.  For sequence s with length seq_lens[s], writes
+ * out[(cu[s] * heads + h * seq_lens[s] + t) * head_dim ...] for every head h
+ * and t < seq_lens[s], cu = exclusive prefix sum of seq_lens (sequences
+ * packed back to back, each [heads][len][head_dim]).  Row t comes from block
+ * block_tables[s * block_table_stride + t / block_size], slot t % block_size.
+ * A quantised pool dequantises with the dequantize_group math
+ * (quantized_cache.rs:278-296: code * scale + zero, f32, no FMA) and rounds
+ * to cfg.dtype.  num_seqs <= RMLX_MAX_SEQS_PER_LAUNCH. */
+#define RMLX_MAX_SEQS_PER_LAUNCH 8192
+RMLX_API rmlx_status rmlx_kv_gather(rmlx_kv_pool* p, int32_t layer, const int32_t* block_tables, int32_t block_table_stride,
+                           const int32_t* seq_lens, int32_t num_seqs, void* out_k, void* out_v, void* stream);
+
+/* Block copy for copy-on-write / fork: every tile of block src[i] is copied
+ * to block dst[i] (all layers, K and V, all heads of the pool).  src/dst are
+ * device arrays of n ids; the dst set must not intersect the src set.  This
+ * moves the bytes that PagedCacheManager::copy_on_write (paged_cache.rs:
+ * 197-224) leaves to the GPU-side cache. */
+RMLX_API rmlx_status rmlx_kv_copy_blocks(rmlx_kv_pool* p, const int32_t* src, const int32_t* dst, int32_t n, void* stream);
+
+/* Pack blocks ids[0..n) into a contiguous device staging buffer of
+ * n * block_bytes (block-major), and the inverse.  Used for cross-GPU block
+ * migration over NCCL. */
+RMLX_API rmlx_status rmlx_kv_pack_blocks(rmlx_kv_pool* p, const int32_t* ids, int32_t n, void* staging, void* stream);
+RMLX_API rmlx_status rmlx_kv_unpack_blocks(rmlx_kv_pool* p, const int32_t* ids, int32_t n, const void* staging,
+                                  void* stream);
+
+/* ======================================================================
+ * Prefix-block chain hash (device).  The reference accepts caller-supplied
+ * block hashes (PagedCacheManager::register_hash, paged_cache.rs:265-272)
+ * and computes none; this defines them.  For request r with tokens
+ * tokens[cu_tokens[r] .. cu_tokens[r+1]), block b covers tokens
+ * [b*block_size, min((b+1)*block_size, n)) and
+ *   hash[b] = XXH64(le64(hash[b-1]) || le32(tokens of block b), seed 0),
+ * hash[-1] = root_hashes[r].  Hashes go to out[cu_blocks[r] + b] with
+ * cu_blocks[r+1] - cu_blocks[r] = ceil(n / block_size).  All arrays are
+ * device arrays. */
+RMLX_API rmlx_status rmlx_hash_block_chains(const uint32_t* tokens, const int64_t* cu_tokens, const uint64_t* root_hashes,
+                                   int32_t num_requests, int32_t block_size, const int64_t* cu_blocks,
+                                   uint64_t* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* RMLX_KV_H */

@@ -1,0 +1,72 @@
+// Device-side helpers shared by the rmlx_kv CUDA sources (sm_100a).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "common.h"
+
+namespace rmlx {
+
+// Error bits latched into a pool's device error word.
+enum : int32_t {
+  DEV_ERR_SLOT = 1,   // slot_mapping entry >= num_blocks * block_size
+  DEV_ERR_BLOCK = 2,  // block-table / copy id outside [0, num_blocks)
+};
+
+// 16-byte streaming load through the non-coherent path without L1
+// allocation: every byte of the pool and of the inputs is read once per
+// launch, so nothing is worth keeping in L1.
+__device__ __forceinline__ uint4 ld_stream(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+// 16-byte store with the evict-first (streaming) policy: gathered rows are
+// consumed by the next kernel or copied out, not re-read by this one.
+__device__ __forceinline__ void st_stream(void* p, uint4 v) {
+  asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+// A warp copies n16 16-byte chunks from src to dst, 8 chunks per lane in
+// flight (4 KiB per warp per round).
+__device__ __forceinline__ void warp_copy(const uint8_t* src, uint8_t* dst, int n16, int lane) {
+  for (int base = 0; base < n16; base += 256) {
+    uint4 r[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      int c = base + lane + 32 * j;
+      if (c < n16) r[j] = ld_stream(src + (size_t)c * 16);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      int c = base + lane + 32 * j;
+      if (c < n16) st_stream(dst + (size_t)c * 16, r[j]);
+    }
+  }
+}
+
+// RAII switch of the current device for the duration of an API call.
+struct DeviceGuard {
+  int prev = -1, dev;
+  explicit DeviceGuard(int d) : dev(d) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    if (prev >= 0 && prev != dev) cudaSetDevice(prev);
+  }
+};
+
+inline rmlx_status cuda_check(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return RMLX_OK;
+  return fail(RMLX_E_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+}  // namespace rmlx

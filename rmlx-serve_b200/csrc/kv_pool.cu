@@ -1,0 +1,757 @@
+// Paged KV pool on one B200: append (reshape-and-cache), block-table gather,
+// fused group-affine quantise-on-append / dequantise-on-gather, block copy
+// (copy-on-write / fork) and pack/unpack for migration.
+//
+// Reference semantics:
+//   * append/gather move rows exactly like RotatingKVCache::append and
+//     get_logical_order (crates/rmlx-serve-cache/src/rotating_cache.rs:
+//     126-136, 162-197), with the row's position taken from a block table
+//     instead of a ring buffer;
+//   * the quantiser is quantize_group (quantized_cache.rs:232-273) applied
+//     to each head_dim/group_size slice of a row: f32 min/max folds, scale =
+//     range / (2^bits - 1) or 1.0 for a flat group, code = round-half-away(
+//     (v - min) / scale) clamped, 4-bit codes packed low nibble first;
+//   * the dequantiser is dequantize_group (:278-296): code * scale + zero as
+//     a rounded multiply followed by a rounded add (no FMA), then rounded to
+//     the output type.
+//
+// All kernels are HBM-bandwidth bound: 16-byte vector loads and stores,
+// every warp streaming whole 4 KiB tiles, persistent grids sized from the
+// SM count.  Tensor cores are not used (nothing here is a contraction).
+#include <algorithm>
+#include <new>
+
+#include "device_common.cuh"
+
+namespace rmlx {
+
+struct PoolGeo {
+  uint8_t* base;
+  int64_t tile_bytes;
+  int32_t layers, heads, bs, nblocks;
+  int32_t row_bytes, meta_row_bytes;
+  __device__ __forceinline__ int64_t tile_off(int64_t blk, int l, int kv, int h) const {
+    return (((blk * layers + l) * 2 + kv) * heads + h) * tile_bytes;
+  }
+};
+
+// ---------------------------------------------------------------------------
+// Append (plain): one thread per 16-byte chunk of a (layer, token, kv, head)
+// row.  Consecutive threads walk a row, then the next head, so both the
+// [token][head][dim] source and the head-contiguous tiles are streamed.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) append_rows_kernel(PoolGeo g, int l0, int nl, const uint8_t* __restrict__ k,
+                                                          const uint8_t* __restrict__ v, int64_t ls, int64_t ts,
+                                                          int64_t hs, const int32_t* __restrict__ slots, int T,
+                                                          int cpr, int32_t* err) {
+  const int64_t total = (int64_t)nl * T * 2 * g.heads * cpr;
+  const int64_t cap = (int64_t)g.nblocks * g.bs;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    int c = (int)(i % cpr);
+    int64_t r = i / cpr;
+    int h = (int)(r % g.heads);
+    r /= g.heads;
+    int kv = (int)(r & 1);
+    r >>= 1;
+    int t = (int)(r % T);
+    int l = (int)(r / T);
+    int32_t s = __ldg(slots + t);
+    if (s < 0) continue;
+    if (s >= cap) {
+      if (c == 0) atomicOr(err, DEV_ERR_SLOT);
+      continue;
+    }
+    int blk = s / g.bs, off = s % g.bs;
+    const uint8_t* src = (kv ? v : k) + l * ls + t * ts + h * hs + c * 16;
+    uint8_t* dst = g.base + g.tile_off(blk, l0 + l, kv, h) + (int64_t)off * g.row_bytes + c * 16;
+    st_stream(dst, ld_stream(src));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Per-CTA prologue of the gathers: exclusive prefix sums of blocks per
+// sequence (cub) and of tokens (cut) over seq_lens, into shared memory.
+// ---------------------------------------------------------------------------
+__device__ void scan_seq_lens(const int32_t* __restrict__ lens, int n, int bs, int32_t* cub, int32_t* cut) {
+  __shared__ int32_t wsb[32], wst[32];
+  const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, w = tid >> 5, nw = nt >> 5;
+  const int per = (n + nt - 1) / nt;
+  const int beg = min(n, tid * per), end = min(n, beg + per);
+  int32_t sb = 0, st = 0;
+  for (int i = beg; i < end; ++i) {
+    int32_t L = max(__ldg(lens + i), 0);
+    sb += (L + bs - 1) / bs;
+    st += L;
+  }
+  int32_t xb = sb, xt = st;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    int32_t yb = __shfl_up_sync(0xffffffffu, xb, o), yt = __shfl_up_sync(0xffffffffu, xt, o);
+    if (lane >= o) {
+      xb += yb;
+      xt += yt;
+    }
+  }
+  if (lane == 31) {
+    wsb[w] = xb;
+    wst[w] = xt;
+  }
+  __syncthreads();
+  if (w == 0) {
+    int32_t vb = lane < nw ? wsb[lane] : 0, vt = lane < nw ? wst[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int32_t yb = __shfl_up_sync(0xffffffffu, vb, o), yt = __shfl_up_sync(0xffffffffu, vt, o);
+      if (lane >= o) {
+        vb += yb;
+        vt += yt;
+      }
+    }
+    wsb[lane] = vb;
+    wst[lane] = vt;
+  }
+  __syncthreads();
+  int32_t pb = xb - sb + (w ? wsb[w - 1] : 0), pt = xt - st + (w ? wst[w - 1] : 0);
+  for (int i = beg; i < end; ++i) {
+    cub[i] = pb;
+    cut[i] = pt;
+    int32_t L = max(__ldg(lens + i), 0);
+    pb += (L + bs - 1) / bs;
+    pt += L;
+  }
+  if (tid == 0) {
+    cub[n] = wsb[nw - 1];
+    cut[n] = wst[nw - 1];
+  }
+  __syncthreads();
+}
+
+// Largest s in [0, n) with cub[s] <= gi (cub is non-decreasing, cub[0] = 0).
+__device__ __forceinline__ int find_seq(const int32_t* cub, int n, int64_t gi) {
+  int lo = 0, hi = n;  // invariant: cub[lo] <= gi < cub[hi]
+  while (hi - lo > 1) {
+    int mid = (lo + hi) >> 1;
+    if (cub[mid] <= gi) lo = mid;
+    else hi = mid;
+  }
+  return lo;
+}
+
+// ---------------------------------------------------------------------------
+// Gather (plain): persistent CTAs; one warp per (sequence block, kv, head)
+// tile.  Units are ordered with the head fastest so that consecutive warps
+// read the adjacent head tiles of one pool block; each full tile lands as
+// one contiguous block_size * row_bytes run in the [seq][head][len][dim]
+// output.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) gather_rows_kernel(PoolGeo g, int layer, const int32_t* __restrict__ bt,
+                                                          int bt_stride, const int32_t* __restrict__ lens, int nseq,
+                                                          uint8_t* __restrict__ ok, uint8_t* __restrict__ ov,
+                                                          int32_t* err) {
+  extern __shared__ int32_t smem[];
+  int32_t* cub = smem;
+  int32_t* cut = smem + nseq + 1;
+  scan_seq_lens(lens, nseq, g.bs, cub, cut);
+  const int64_t units = (int64_t)cub[nseq] * 2 * g.heads;
+  const int lane = threadIdx.x & 31;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t u = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; u < units; u += nwarps) {
+    int h = (int)(u % g.heads);
+    int64_t q = u / g.heads;
+    int kv = (int)(q & 1);
+    int64_t gi = q >> 1;
+    int s = find_seq(cub, nseq, gi);
+    int b = (int)(gi - cub[s]);
+    int L = cut[s + 1] - cut[s];
+    int nrows = min(g.bs, L - b * g.bs);
+    int32_t blk = __ldg(bt + (int64_t)s * bt_stride + b);
+    if (blk < 0 || blk >= g.nblocks) {
+      if (lane == 0) atomicOr(err, DEV_ERR_BLOCK);
+      continue;
+    }
+    const uint8_t* src = g.base + g.tile_off(blk, layer, kv, h);
+    uint8_t* dst = (kv ? ov : ok) + ((int64_t)cut[s] * g.heads + (int64_t)h * L + (int64_t)b * g.bs) * g.row_bytes;
+    warp_copy(src, dst, nrows * g.row_bytes / 16, lane);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Element conversions for the quantised paths.
+// ---------------------------------------------------------------------------
+template <int DT>  // rmlx_dtype
+struct Elem;
+template <>
+struct Elem<RMLX_F32> {
+  static constexpr int size = 4;
+  // 8 consecutive elements -> f32
+  __device__ __forceinline__ static void load8(const uint8_t* p, float* f) {
+    uint4 a = ld_stream(p), b = ld_stream(p + 16);
+    f[0] = __uint_as_float(a.x), f[1] = __uint_as_float(a.y), f[2] = __uint_as_float(a.z), f[3] = __uint_as_float(a.w);
+    f[4] = __uint_as_float(b.x), f[5] = __uint_as_float(b.y), f[6] = __uint_as_float(b.z), f[7] = __uint_as_float(b.w);
+  }
+  __device__ __forceinline__ static void store8(uint8_t* p, const float* f) {
+    st_stream(p, make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]), __float_as_uint(f[3])));
+    st_stream(p + 16,
+              make_uint4(__float_as_uint(f[4]), __float_as_uint(f[5]), __float_as_uint(f[6]), __float_as_uint(f[7])));
+  }
+};
+template <>
+struct Elem<RMLX_F16> {
+  static constexpr int size = 2;
+  __device__ __forceinline__ static void load8(const uint8_t* p, float* f) {
+    uint4 a = ld_stream(p);
+    const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
+      float2 x = __half22float2(h);
+      f[2 * i] = x.x;
+      f[2 * i + 1] = x.y;
+    }
+  }
+  __device__ __forceinline__ static uint32_t pack(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  __device__ __forceinline__ static void store8(uint8_t* p, const float* f) {
+    st_stream(p, make_uint4(pack(f[0], f[1]), pack(f[2], f[3]), pack(f[4], f[5]), pack(f[6], f[7])));
+  }
+};
+template <>
+struct Elem<RMLX_BF16> {
+  static constexpr int size = 2;
+  __device__ __forceinline__ static void load8(const uint8_t* p, float* f) {
+    uint4 a = ld_stream(p);
+    const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      f[2 * i] = __uint_as_float(w[i] << 16);
+      f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+  }
+  __device__ __forceinline__ static uint32_t pack(float a, float b) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  __device__ __forceinline__ static void store8(uint8_t* p, const float* f) {
+    st_stream(p, make_uint4(pack(f[0], f[1]), pack(f[2], f[3]), pack(f[4], f[5]), pack(f[6], f[7])));
+  }
+};
+
+// Rust `x.round().clamp(0.0, qmax) as u8`: half-away rounding, clamp that
+// passes NaN through, saturating cast with NaN -> 0.
+__device__ __forceinline__ uint32_t quant_code(float v, float mn, float scale, float qmax) {
+  float x = roundf(__fdiv_rn(__fsub_rn(v, mn), scale));
+  if (x < 0.0f) x = 0.0f;
+  if (x > qmax) x = qmax;
+  return (x == x) ? (uint32_t)x : 0u;
+}
+
+// ---------------------------------------------------------------------------
+// Quantise-on-append: one thread per 8 elements of a row; a group of
+// group_size elements is group_size/8 adjacent lanes (a power of two <= 32,
+// aligned, never crossing a warp), reduced with xor shuffles.
+// ---------------------------------------------------------------------------
+template <int IN_DT, int BITS, bool META_F32>
+__global__ void __launch_bounds__(256) append_quant_kernel(PoolGeo g, int l0, int nl, const uint8_t* __restrict__ k,
+                                                           const uint8_t* __restrict__ v, int64_t ls, int64_t ts,
+                                                           int64_t hs, const int32_t* __restrict__ slots, int T,
+                                                           int hd, int tpg, int32_t* err) {
+  using E = Elem<IN_DT>;
+  const int cpr = hd / 8;
+  const int64_t total = (int64_t)nl * T * 2 * g.heads * cpr;
+  const int64_t cap = (int64_t)g.nblocks * g.bs;
+  const float qmax = (float)((1u << BITS) - 1);
+  const int lane = threadIdx.x & 31;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t wb = blockIdx.x * (int64_t)blockDim.x + (threadIdx.x & ~31); wb < total; wb += stride) {
+    const int64_t i = wb + lane;
+    bool valid = i < total;
+    int c = 0, h = 0, kv = 0, t = 0, l = 0;
+    int32_t s = -1;
+    if (valid) {
+      c = (int)(i % cpr);
+      int64_t r = i / cpr;
+      h = (int)(r % g.heads);
+      r /= g.heads;
+      kv = (int)(r & 1);
+      r >>= 1;
+      t = (int)(r % T);
+      l = (int)(r / T);
+      s = __ldg(slots + t);
+      if (s >= cap) {
+        if (c == 0) atomicOr(err, DEV_ERR_SLOT);
+        s = -1;
+      }
+      valid = s >= 0;
+    }
+    float f[8];
+    if (valid) {
+      E::load8((kv ? v : k) + l * ls + t * ts + h * hs + (int64_t)c * 8 * E::size, f);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) f[e] = 0.0f;
+    }
+    float mx = -INFINITY, mn = INFINITY;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) mx = fmaxf(mx, f[e]);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) mn = fminf(mn, f[e]);
+    for (int o = 1; o < tpg; o <<= 1) {
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+    }
+    if (!valid) continue;
+    const float range = __fsub_rn(mx, mn);
+    const float scale = (range == 0.0f) ? 1.0f : __fdiv_rn(range, qmax);
+    const int blk = s / g.bs, off = s % g.bs;
+    uint8_t* tile = g.base + g.tile_off(blk, l0 + l, kv, h);
+    uint8_t* code_row = tile + (int64_t)off * g.row_bytes;
+    if (BITS == 8) {
+      uint32_t lo = 0, hi = 0;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) lo |= quant_code(f[e], mn, scale, qmax) << (8 * e);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) hi |= quant_code(f[4 + e], mn, scale, qmax) << (8 * e);
+      *reinterpret_cast<uint2*>(code_row + c * 8) = make_uint2(lo, hi);
+    } else {
+      uint32_t w = 0;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        uint32_t a = quant_code(f[2 * e], mn, scale, qmax), b = quant_code(f[2 * e + 1], mn, scale, qmax);
+        w |= (a | (b << 4)) << (8 * e);
+      }
+      *reinterpret_cast<uint32_t*>(code_row + c * 4) = w;
+    }
+    if ((c & (tpg - 1)) == 0) {
+      const int q = c / tpg;
+      uint8_t* meta_row = tile + (int64_t)g.bs * g.row_bytes + (int64_t)off * g.meta_row_bytes;
+      if (META_F32) {
+        reinterpret_cast<float*>(meta_row)[2 * q] = scale;
+        reinterpret_cast<float*>(meta_row)[2 * q + 1] = mn;
+      } else {
+        reinterpret_cast<__half2*>(meta_row)[q] = __halves2half2(__float2half_rn(scale), __float2half_rn(mn));
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Dequantise-on-gather: persistent CTAs, one warp per tile as in the plain
+// gather.  A lane decodes one 16-byte chunk of codes (16 codes at 8 bits,
+// 32 at 4 bits).  ONE_GROUP: group_size is a multiple of the codes in a
+// chunk, so one (scale, zero) pair serves the whole chunk.
+// ---------------------------------------------------------------------------
+template <int BITS, int OUT_DT, bool META_F32, bool ONE_GROUP>
+__global__ void __launch_bounds__(256) gather_dequant_kernel(PoolGeo g, int layer, const int32_t* __restrict__ bt,
+                                                             int bt_stride, const int32_t* __restrict__ lens,
+                                                             int nseq, uint8_t* __restrict__ ok,
+                                                             uint8_t* __restrict__ ov, int hd, int gs_log2,
+                                                             int32_t* err) {
+  using E = Elem<OUT_DT>;
+  constexpr int EPC = BITS == 8 ? 16 : 32;  // elements per 16-byte code chunk
+  constexpr int U = 4;                      // chunks per lane in flight
+  extern __shared__ int32_t smem[];
+  int32_t* cub = smem;
+  int32_t* cut = smem + nseq + 1;
+  scan_seq_lens(lens, nseq, g.bs, cub, cut);
+  const int64_t units = (int64_t)cub[nseq] * 2 * g.heads;
+  const int lane = threadIdx.x & 31;
+  const int cpr = g.row_bytes / 16;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t u = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; u < units; u += nwarps) {
+    int h = (int)(u % g.heads);
+    int64_t q = u / g.heads;
+    int kv = (int)(q & 1);
+    int64_t gi = q >> 1;
+    int s = find_seq(cub, nseq, gi);
+    int b = (int)(gi - cub[s]);
+    int L = cut[s + 1] - cut[s];
+    int nrows = min(g.bs, L - b * g.bs);
+    int32_t blk = __ldg(bt + (int64_t)s * bt_stride + b);
+    if (blk < 0 || blk >= g.nblocks) {
+      if (lane == 0) atomicOr(err, DEV_ERR_BLOCK);
+      continue;
+    }
+    const uint8_t* tile = g.base + g.tile_off(blk, layer, kv, h);
+    const uint8_t* meta = tile + (int64_t)g.bs * g.row_bytes;
+    uint8_t* out = (kv ? ov : ok) + ((int64_t)cut[s] * g.heads + (int64_t)h * L + (int64_t)b * g.bs) * hd * E::size;
+    const int n16 = nrows * cpr;
+    for (int base = 0; base < n16; base += 32 * U) {
+      uint4 cw[U];
+#pragma unroll
+      for (int j = 0; j < U; ++j) {
+        int idx = base + lane + 32 * j;
+        if (idx < n16) cw[j] = ld_stream(tile + (int64_t)idx * 16);
+      }
+#pragma unroll
+      for (int j = 0; j < U; ++j) {
+        int idx = base + lane + 32 * j;
+        if (idx >= n16) continue;
+        const int r = idx / cpr, e0 = (idx - r * cpr) * EPC;
+        const uint8_t* mrow = meta + (int64_t)r * g.meta_row_bytes;
+        const uint32_t w[4] = {cw[j].x, cw[j].y, cw[j].z, cw[j].w};
+        uint8_t* orow = out + ((int64_t)r * hd + e0) * E::size;
+        float sc = 0.0f, zr = 0.0f;
+        if (ONE_GROUP) {
+          const int gq = e0 >> gs_log2;
+          if (META_F32) {
+            sc = __ldg(reinterpret_cast<const float*>(mrow) + 2 * gq);
+            zr = __ldg(reinterpret_cast<const float*>(mrow) + 2 * gq + 1);
+          } else {
+            float2 m = __half22float2(__ldg(reinterpret_cast<const __half2*>(mrow) + gq));
+            sc = m.x;
+            zr = m.y;
+          }
+        }
+#pragma unroll
+        for (int o8 = 0; o8 < EPC / 8; ++o8) {
+          float f[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const int el = o8 * 8 + e;  // element within the chunk
+            uint32_t code;
+            if (BITS == 8) code = (w[el >> 2] >> (8 * (el & 3))) & 0xffu;
+            else code = (w[el >> 3] >> (4 * (el & 7))) & 0xfu;
+            if (!ONE_GROUP) {
+              const int gq = (e0 + el) >> gs_log2;
+              if (META_F32) {
+                sc = __ldg(reinterpret_cast<const float*>(mrow) + 2 * gq);
+                zr = __ldg(reinterpret_cast<const float*>(mrow) + 2 * gq + 1);
+              } else {
+                float2 m = __half22float2(__ldg(reinterpret_cast<const __half2*>(mrow) + gq));
+                sc = m.x;
+                zr = m.y;
+              }
+            }
+            f[e] = __fadd_rn(__fmul_rn((float)code, sc), zr);
+          }
+          E::store8(orow + o8 * 8 * E::size, f);
+        }
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Block copy / pack / unpack: one warp per 4 KiB segment of a block.
+//   mode 0: pool[dst[i]] = pool[src[i]]
+//   mode 1: staging[i]   = pool[src[i]]       (pack)
+//   mode 2: pool[src[i]] = staging[i]         (unpack)
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) copy_blocks_kernel(uint8_t* base, int64_t block_bytes, int nblocks,
+                                                          const int32_t* __restrict__ src,
+                                                          const int32_t* __restrict__ dst, int n, int mode,
+                                                          uint8_t* staging, int32_t* err) {
+  const int64_t segs = (block_bytes + 4095) / 4096;
+  const int64_t units = (int64_t)n * segs;
+  const int lane = threadIdx.x & 31;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t u = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; u < units; u += nwarps) {
+    const int i = (int)(u / segs);
+    const int64_t off = (u - (int64_t)i * segs) * 4096;
+    const int bytes = (int)min((int64_t)4096, block_bytes - off);
+    const int32_t a = __ldg(src + i);
+    const int32_t b = mode == 0 ? __ldg(dst + i) : 0;
+    if (a < 0 || a >= nblocks || b < 0 || b >= nblocks) {
+      if (lane == 0) atomicOr(err, DEV_ERR_BLOCK);
+      continue;
+    }
+    const uint8_t* sp;
+    uint8_t* dp;
+    if (mode == 0) {
+      sp = base + (int64_t)a * block_bytes + off;
+      dp = base + (int64_t)b * block_bytes + off;
+    } else if (mode == 1) {
+      sp = base + (int64_t)a * block_bytes + off;
+      dp = staging + (int64_t)i * block_bytes + off;
+    } else {
+      sp = staging + (int64_t)i * block_bytes + off;
+      dp = base + (int64_t)a * block_bytes + off;
+    }
+    warp_copy(sp, dp, bytes / 16, lane);
+  }
+}
+
+static int dtype_size(int dt) { return dt == RMLX_F32 ? 4 : 2; }
+static bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
+
+}  // namespace rmlx
+
+using namespace rmlx;
+
+struct rmlx_kv_pool {
+  rmlx_pool_config cfg;
+  int device = 0;
+  uint8_t* base = nullptr;
+  int32_t* err = nullptr;
+  size_t bytes = 0, tile_bytes = 0, block_bytes = 0, row_bytes = 0, meta_row_bytes = 0;
+  int num_sms = 148;
+  PoolGeo geo() const {
+    PoolGeo g;
+    g.base = base;
+    g.tile_bytes = (int64_t)tile_bytes;
+    g.layers = cfg.num_layers;
+    g.heads = cfg.num_kv_heads;
+    g.bs = cfg.block_size;
+    g.nblocks = cfg.num_blocks;
+    g.row_bytes = (int32_t)row_bytes;
+    g.meta_row_bytes = (int32_t)meta_row_bytes;
+    return g;
+  }
+};
+
+namespace {
+
+bool is_pow2(int x) { return x > 0 && (x & (x - 1)) == 0; }
+int log2i(int x) {
+  int r = 0;
+  while ((1 << r) < x) ++r;
+  return r;
+}
+
+// Persistent grid: resident CTAs per SM x SM count.
+template <typename K>
+int persistent_grid(K kernel, int threads, size_t smem, int num_sms) {
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess || per_sm < 1)
+    per_sm = 1;
+  return per_sm * num_sms;
+}
+
+template <typename K>
+rmlx_status prepare_smem(K kernel, size_t smem) {
+  if (smem <= 48 * 1024) return RMLX_OK;
+  return cuda_check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                    "cudaFuncSetAttribute");
+}
+
+// Dispatch tables for the templated quantised kernels.
+using AppendQuantFn = void (*)(PoolGeo, int, int, const uint8_t*, const uint8_t*, int64_t, int64_t, int64_t,
+                               const int32_t*, int, int, int, int32_t*);
+template <int IN, int BITS, bool MF32>
+AppendQuantFn aq() {
+  return append_quant_kernel<IN, BITS, MF32>;
+}
+AppendQuantFn pick_append_quant(int in_dt, int bits, bool mf32) {
+  static const AppendQuantFn t[3][2][2] = {
+      {{aq<0, 4, false>(), aq<0, 4, true>()}, {aq<0, 8, false>(), aq<0, 8, true>()}},
+      {{aq<1, 4, false>(), aq<1, 4, true>()}, {aq<1, 8, false>(), aq<1, 8, true>()}},
+      {{aq<2, 4, false>(), aq<2, 4, true>()}, {aq<2, 8, false>(), aq<2, 8, true>()}},
+  };
+  return t[in_dt][bits == 8][mf32];
+}
+
+using GatherDqFn = void (*)(PoolGeo, int, const int32_t*, int, const int32_t*, int, uint8_t*, uint8_t*, int, int,
+                            int32_t*);
+template <int BITS, int OUT, bool MF32, bool ONE>
+GatherDqFn gd() {
+  return gather_dequant_kernel<BITS, OUT, MF32, ONE>;
+}
+GatherDqFn pick_gather_dequant(int bits, int out_dt, bool mf32, bool one) {
+#define GD_ROW(B, O) {{gd<B, O, false, false>(), gd<B, O, false, true>()}, {gd<B, O, true, false>(), gd<B, O, true, true>()}}
+  static const GatherDqFn t[2][3][2][2] = {
+      {GD_ROW(4, 0), GD_ROW(4, 1), GD_ROW(4, 2)},
+      {GD_ROW(8, 0), GD_ROW(8, 1), GD_ROW(8, 2)},
+  };
+#undef GD_ROW
+  return t[bits == 8][out_dt][mf32][one];
+}
+
+}  // namespace
+
+extern "C" {
+
+rmlx_status rmlx_kv_pool_new(const rmlx_pool_config* cfg, int device, rmlx_kv_pool** out) {
+  if (!cfg || !out) return fail(RMLX_E_BAD_ARG, "NULL cfg or out");
+  *out = nullptr;
+  const rmlx_pool_config c = *cfg;
+  if (c.num_layers <= 0 || c.num_kv_heads <= 0 || c.head_dim <= 0 || c.block_size <= 0 || c.num_blocks <= 0)
+    return fail(RMLX_E_BAD_ARG, "pool dimensions must be positive");
+  if (c.dtype < RMLX_F32 || c.dtype > RMLX_BF16) return fail(RMLX_E_BAD_ARG, "dtype must be F32, F16 or BF16");
+  if ((int64_t)c.num_blocks * c.block_size > INT32_MAX) return fail(RMLX_E_BAD_ARG, "num_blocks * block_size exceeds int32 slots");
+  rmlx_kv_pool p;
+  p.cfg = c;
+  p.device = device;
+  if (c.quant_bits == 0) {
+    p.row_bytes = (size_t)c.head_dim * dtype_size(c.dtype);
+    if (p.row_bytes % 16) return fail(RMLX_E_BAD_ARG, "head_dim * element size must be a multiple of 16 bytes");
+    p.meta_row_bytes = 0;
+  } else if (c.quant_bits == 4 || c.quant_bits == 8) {
+    if (!is_pow2(c.group_size) || c.group_size < 8 || c.group_size > 256)
+      return fail(RMLX_E_BAD_ARG, "group_size must be a power of two in [8, 256]");
+    if (c.head_dim % c.group_size) return fail(RMLX_E_BAD_ARG, "head_dim must be a multiple of group_size");
+    if (c.meta_dtype != RMLX_F32 && c.meta_dtype != RMLX_F16) return fail(RMLX_E_BAD_ARG, "meta_dtype must be F32 or F16");
+    p.row_bytes = (size_t)c.head_dim * c.quant_bits / 8;
+    if (p.row_bytes % 16) return fail(RMLX_E_BAD_ARG, "head_dim * bits / 8 must be a multiple of 16 bytes");
+    p.meta_row_bytes = (size_t)(c.head_dim / c.group_size) * 2 * dtype_size(c.meta_dtype);
+  } else {
+    return fail(RMLX_E_BAD_ARG, "bits must be 4 or 8, got %d", c.quant_bits);
+  }
+  p.tile_bytes = ((size_t)c.block_size * (p.row_bytes + p.meta_row_bytes) + 15) / 16 * 16;
+  p.block_bytes = p.tile_bytes * c.num_layers * 2 * c.num_kv_heads;
+  p.bytes = p.block_bytes * c.num_blocks;
+  DeviceGuard dg(device);
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) == cudaSuccess && sms > 0) p.num_sms = sms;
+  rmlx_status s = cuda_check(cudaMalloc(&p.base, p.bytes), "cudaMalloc(pool)");
+  if (s != RMLX_OK) return s == RMLX_E_CUDA ? fail(RMLX_E_EXHAUSTED, "%s", rmlx_last_error()) : s;
+  if ((s = cuda_check(cudaMalloc(&p.err, sizeof(int32_t)), "cudaMalloc(err)")) != RMLX_OK) {
+    cudaFree(p.base);
+    return s;
+  }
+  if ((s = cuda_check(cudaMemset(p.base, 0, p.bytes), "cudaMemset(pool)")) != RMLX_OK ||
+      (s = cuda_check(cudaMemset(p.err, 0, sizeof(int32_t)), "cudaMemset(err)")) != RMLX_OK) {
+    cudaFree(p.base);
+    cudaFree(p.err);
+    return s;
+  }
+  *out = new (std::nothrow) rmlx_kv_pool(p);
+  if (!*out) {
+    cudaFree(p.base);
+    cudaFree(p.err);
+    return fail(RMLX_E_EXHAUSTED, "host allocation failed");
+  }
+  return RMLX_OK;
+}
+
+void rmlx_kv_pool_destroy(rmlx_kv_pool* p) {
+  if (!p) return;
+  {
+    DeviceGuard dg(p->device);
+    cudaFree(p->base);
+    cudaFree(p->err);
+  }
+  delete p;
+}
+
+rmlx_status rmlx_kv_pool_layout(const rmlx_kv_pool* p, rmlx_pool_layout* o) {
+  if (!p || !o) return fail(RMLX_E_BAD_ARG, "NULL pool or out");
+  o->base = p->base;
+  o->bytes = p->bytes;
+  o->tile_bytes = p->tile_bytes;
+  o->block_bytes = p->block_bytes;
+  o->row_bytes = p->row_bytes;
+  o->meta_row_bytes = p->meta_row_bytes;
+  return RMLX_OK;
+}
+
+rmlx_status rmlx_kv_pool_check(rmlx_kv_pool* p, int32_t* device_error) {
+  if (!p || !device_error) return fail(RMLX_E_BAD_ARG, "NULL pool or out");
+  DeviceGuard dg(p->device);
+  rmlx_status s = cuda_check(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+  if (s != RMLX_OK) return s;
+  if ((s = cuda_check(cudaMemcpy(device_error, p->err, sizeof(int32_t), cudaMemcpyDeviceToHost), "read error word")) != RMLX_OK)
+    return s;
+  return cuda_check(cudaMemset(p->err, 0, sizeof(int32_t)), "clear error word");
+}
+
+rmlx_status rmlx_kv_pool_read(rmlx_kv_pool* p, size_t offset, size_t nbytes, void* host_dst) {
+  if (!p || (nbytes && !host_dst)) return fail(RMLX_E_BAD_ARG, "NULL pool or destination");
+  if (offset > p->bytes || nbytes > p->bytes - offset) return fail(RMLX_E_RANGE, "read past the end of the pool");
+  if (nbytes == 0) return RMLX_OK;
+  DeviceGuard dg(p->device);
+  return cuda_check(cudaMemcpy(host_dst, p->base + offset, nbytes, cudaMemcpyDeviceToHost), "pool read");
+}
+
+rmlx_status rmlx_kv_pool_write(rmlx_kv_pool* p, size_t offset, size_t nbytes, const void* host_src) {
+  if (!p || (nbytes && !host_src)) return fail(RMLX_E_BAD_ARG, "NULL pool or source");
+  if (offset > p->bytes || nbytes > p->bytes - offset) return fail(RMLX_E_RANGE, "write past the end of the pool");
+  if (nbytes == 0) return RMLX_OK;
+  DeviceGuard dg(p->device);
+  return cuda_check(cudaMemcpy(p->base + offset, host_src, nbytes, cudaMemcpyHostToDevice), "pool write");
+}
+
+rmlx_status rmlx_kv_append(rmlx_kv_pool* p, int32_t layer_begin, int32_t num_layers, const void* k, const void* v,
+                           int64_t layer_stride, int64_t token_stride, int64_t head_stride, const int32_t* slots,
+                           int32_t T, void* stream) {
+  if (!p) return fail(RMLX_E_BAD_ARG, "NULL pool");
+  const rmlx_pool_config& c = p->cfg;
+  if (layer_begin < 0 || num_layers < 0 || layer_begin + num_layers > c.num_layers)
+    return fail(RMLX_E_RANGE, "layers [%d, %d) outside the pool's %d layers", layer_begin, layer_begin + num_layers,
+                c.num_layers);
+  if (T < 0) return fail(RMLX_E_BAD_ARG, "num_tokens < 0");
+  if (T == 0 || num_layers == 0) return RMLX_OK;
+  if (!k || !v || !slots) return fail(RMLX_E_BAD_ARG, "NULL k, v or slot_mapping");
+  const int es = dtype_size(c.dtype);
+  const int64_t ls = layer_stride * es, ts = token_stride * es, hs = head_stride * es;
+  if (!aligned16(k) || !aligned16(v) || (ls % 16) || (ts % 16) || (hs % 16))
+    return fail(RMLX_E_BAD_ARG, "k/v pointers and strides must be 16-byte aligned");
+  DeviceGuard dg(p->device);
+  cudaStream_t st = (cudaStream_t)stream;
+  PoolGeo g = p->geo();
+  const uint8_t* kb = (const uint8_t*)k;
+  const uint8_t* vb = (const uint8_t*)v;
+  if (c.quant_bits == 0) {
+    const int cpr = (int)(p->row_bytes / 16);
+    const int64_t total = (int64_t)num_layers * T * 2 * c.num_kv_heads * cpr;
+    const int grid = (int)std::min<int64_t>((total + 255) / 256, (int64_t)p->num_sms * 16);
+    append_rows_kernel<<<grid, 256, 0, st>>>(g, layer_begin, num_layers, kb, vb, ls, ts, hs, slots, T, cpr, p->err);
+  } else {
+    const int tpg = c.group_size / 8;
+    const int64_t total = (int64_t)num_layers * T * 2 * c.num_kv_heads * (c.head_dim / 8);
+    const int grid = (int)std::min<int64_t>((total + 255) / 256, (int64_t)p->num_sms * 16);
+    AppendQuantFn fn = pick_append_quant(c.dtype, c.quant_bits, c.meta_dtype == RMLX_F32);
+    fn<<<grid, 256, 0, st>>>(g, layer_begin, num_layers, kb, vb, ls, ts, hs, slots, T, c.head_dim, tpg, p->err);
+  }
+  return cuda_check(cudaGetLastError(), "append launch");
+}
+
+rmlx_status rmlx_kv_gather(rmlx_kv_pool* p, int32_t layer, const int32_t* bt, int32_t bt_stride, const int32_t* lens,
+                           int32_t nseq, void* out_k, void* out_v, void* stream) {
+  if (!p) return fail(RMLX_E_BAD_ARG, "NULL pool");
+  const rmlx_pool_config& c = p->cfg;
+  if (layer < 0 || layer >= c.num_layers) return fail(RMLX_E_RANGE, "layer %d outside the pool's %d layers", layer, c.num_layers);
+  if (nseq < 0 || nseq > RMLX_MAX_SEQS_PER_LAUNCH)
+    return fail(RMLX_E_BAD_ARG, "num_seqs %d outside [0, %d]", nseq, RMLX_MAX_SEQS_PER_LAUNCH);
+  if (nseq == 0) return RMLX_OK;
+  if (!bt || !lens || !out_k || !out_v) return fail(RMLX_E_BAD_ARG, "NULL block_tables, seq_lens or outputs");
+  if (bt_stride < 0) return fail(RMLX_E_BAD_ARG, "block_table_stride < 0");
+  if (!aligned16(out_k) || !aligned16(out_v)) return fail(RMLX_E_BAD_ARG, "outputs must be 16-byte aligned");
+  DeviceGuard dg(p->device);
+  cudaStream_t st = (cudaStream_t)stream;
+  PoolGeo g = p->geo();
+  const size_t smem = (size_t)(nseq + 1) * 2 * sizeof(int32_t);
+  rmlx_status s;
+  if (c.quant_bits == 0) {
+    if ((s = prepare_smem(gather_rows_kernel, smem)) != RMLX_OK) return s;
+    const int grid = persistent_grid(gather_rows_kernel, 256, smem, p->num_sms);
+    gather_rows_kernel<<<grid, 256, smem, st>>>(g, layer, bt, bt_stride, lens, nseq, (uint8_t*)out_k, (uint8_t*)out_v,
+                                                p->err);
+  } else {
+    const int epc = c.quant_bits == 8 ? 16 : 32;
+    GatherDqFn fn = pick_gather_dequant(c.quant_bits, c.dtype, c.meta_dtype == RMLX_F32, c.group_size % epc == 0);
+    if ((s = prepare_smem(fn, smem)) != RMLX_OK) return s;
+    const int grid = persistent_grid(fn, 256, smem, p->num_sms);
+    fn<<<grid, 256, smem, st>>>(g, layer, bt, bt_stride, lens, nseq, (uint8_t*)out_k, (uint8_t*)out_v, c.head_dim,
+                                log2i(c.group_size), p->err);
+  }
+  return cuda_check(cudaGetLastError(), "gather launch");
+}
+
+static rmlx_status launch_copy(rmlx_kv_pool* p, const int32_t* a, const int32_t* b, int32_t n, int mode,
+                               uint8_t* staging, void* stream) {
+  if (!p) return fail(RMLX_E_BAD_ARG, "NULL pool");
+  if (n < 0) return fail(RMLX_E_BAD_ARG, "n < 0");
+  if (n == 0) return RMLX_OK;
+  if (!a || (mode == 0 && !b) || (mode != 0 && !staging)) return fail(RMLX_E_BAD_ARG, "NULL id array or staging");
+  if (mode != 0 && !aligned16(staging)) return fail(RMLX_E_BAD_ARG, "staging must be 16-byte aligned");
+  DeviceGuard dg(p->device);
+  const int64_t units = (int64_t)n * (((int64_t)p->block_bytes + 4095) / 4096);
+  const int grid = (int)std::min<int64_t>((units + 7) / 8, (int64_t)p->num_sms * 8);
+  copy_blocks_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(p->base, (int64_t)p->block_bytes, p->cfg.num_blocks, a,
+                                                             b, n, mode, staging, p->err);
+  return cuda_check(cudaGetLastError(), "copy_blocks launch");
+}
+
+rmlx_status rmlx_kv_copy_blocks(rmlx_kv_pool* p, const int32_t* src, const int32_t* dst, int32_t n, void* stream) {
+  return launch_copy(p, src, dst, n, 0, nullptr, stream);
+}
+rmlx_status rmlx_kv_pack_blocks(rmlx_kv_pool* p, const int32_t* ids, int32_t n, void* staging, void* stream) {
+  return launch_copy(p, ids, nullptr, n, 1, (uint8_t*)staging, stream);
+}
+rmlx_status rmlx_kv_unpack_blocks(rmlx_kv_pool* p, const int32_t* ids, int32_t n, const void* staging, void* stream) {
+  return launch_copy(p, ids, nullptr, n, 2, (uint8_t*)staging, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,122 @@
+"""GPU parity: group-affine quantise-on-append and dequantise-on-gather.
+
+Codes, scales and zeros must be bit-identical to the oracle's restatement of
+quantize_group (quantized_cache.rs:232-273); dequantised rows must be
+bit-identical to dequantize_group's f32 `code * scale + zero`
+(quantized_cache.rs:278-296) rounded to the output type, i.e. within 0.5 ulp
+of the reference's f32 value.  With f16 metadata the codes are still exact
+and the dequantised value is checked against the f32-metadata value with a
+stated bound.
+"""
+import numpy as np
+import pytest
+
+import oracle as orc
+import rmlx_kv
+from helpers import ESIZE, NP_DT, block_tables, rand_rows, slots_for, to_dev, to_host
+
+pytestmark = pytest.mark.gpu
+
+
+def run_quant_case(cuda, L, H, D, bs, N, dt, bits, gs, meta, prompt_lens, new_tokens=1, seed=0, outliers=0.01):
+    import torch
+    rng = np.random.default_rng(seed)
+    lens = np.array(prompt_lens, dtype=np.int64)
+    bt, _ = block_tables(rng, lens, bs, N, extra=new_tokens)
+    g = orc.Geo(L, H, D, bs, N, ESIZE[dt], bits=bits, group_size=gs, meta_bytes=4 if meta == orc.F32 else 2)
+    host = np.zeros(g.pool_bytes(), dtype=np.uint8)
+    pool = rmlx_kv.KVPool(L, H, D, bs, N, dtype=dt, quant_bits=bits, group_size=gs, meta_dtype=meta)
+    assert pool.layout.bytes == host.size
+
+    def append(positions):
+        T = len(positions)
+        if T == 0:
+            return
+        k = rand_rows(rng, (L, T, H, D), dt, outliers)
+        v = rand_rows(rng, (L, T, H, D), dt, outliers)
+        slots = slots_for(bt, bs, positions)
+        assert orc.paged_append_quant(host, g, 0, L, k, v, dt, T * H * D, H * D, D, slots) == 0
+        pool.append(to_dev(k), to_dev(v), to_dev(slots), T)
+
+    append([(s, p) for s in range(len(lens)) for p in range(lens[s])])
+    for step in range(new_tokens):
+        append([(s, int(lens[s]) + step) for s in range(len(lens))])
+    assert pool.check() == 0
+    np.testing.assert_array_equal(pool.read(), host)  # codes + meta bit-exact
+
+    final = (lens + new_tokens).astype(np.int32)
+    tot = int(final.sum()) * H * D
+    npdt = NP_DT[dt]
+    ok = torch.empty(max(tot * ESIZE[dt], 16), dtype=torch.uint8, device=cuda)
+    ov = torch.empty_like(ok)
+    bt_d, lens_d = to_dev(bt), to_dev(final)
+    for layer in range(L):
+        ek = np.zeros(tot, dtype=npdt)
+        ev = np.zeros(tot, dtype=npdt)
+        assert orc.paged_gather_dequant(host, g, layer, bt, bt.shape[1], final, ek, ev, dt) == 0
+        pool.gather(layer, bt_d, bt.shape[1], lens_d, len(final), ok, ov)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(to_host(ok, npdt)[:tot], ek)
+        np.testing.assert_array_equal(to_host(ov, npdt)[:tot], ev)
+    assert pool.check() == 0
+    pool.close()
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+@pytest.mark.parametrize("meta", [orc.F32, orc.F16])
+def test_llama_shape_small_batch(cuda, bits, meta):
+    """8 heads x 128, group 64, bf16, 1% outliers x8 (the quantised-store config), small batch."""
+    run_quant_case(cuda, 2, 8, 128, 16, 128, orc.BF16, bits, 64, meta, [37, 128, 255, 300], seed=11)
+
+
+@pytest.mark.parametrize("dt", [orc.F32, orc.F16])
+@pytest.mark.parametrize("gs", [8, 16, 32, 128])
+def test_group_sizes_and_dtypes(cuda, dt, gs):
+    run_quant_case(cuda, 1, 2, 128, 16, 32, dt, 8 if gs != 16 else 4, gs, orc.F32, [1, 17, 40], seed=12)
+
+
+def test_4bit_small_groups_split_chunks(cuda):
+    """group 8 < 32 codes per 16-byte chunk: per-element group lookup path."""
+    run_quant_case(cuda, 1, 1, 64, 8, 16, orc.BF16, 4, 8, orc.F16, [9, 30], new_tokens=2, seed=13)
+
+
+def test_constant_groups_use_unit_scale(cuda):
+    """range == 0 -> scale 1.0, zero = the value, codes 0 (quantized_cache.rs:242, :368-380)."""
+    import torch
+    L, H, D, bs, N = 1, 1, 64, 4, 4
+    pool = rmlx_kv.KVPool(L, H, D, bs, N, dtype=orc.F32, quant_bits=8, group_size=64)
+    k = np.full((1, 1, H, D), 42.0, dtype=np.float32)
+    pool.append(to_dev(k), to_dev(k), to_dev(np.array([0], dtype=np.int32)), 1)
+    raw = pool.read(0, pool.layout.tile_bytes)
+    assert not raw[:64].any()
+    meta = raw[bs * 64:bs * 64 + 8].view(np.float32)
+    assert meta[0] == 1.0 and meta[1] == 42.0
+    out = torch.empty(D, dtype=torch.float32, device=cuda)
+    out2 = torch.empty_like(out)
+    pool.gather(0, to_dev(np.zeros((1, 1), np.int32)), 1, to_dev(np.array([1], np.int32)), 1, out, out2)
+    assert (out.cpu().numpy() == 42.0).all()
+
+
+def test_f16_meta_error_bound(cuda):
+    """fp16 scale/zero: codes identical to f32 metadata, dequant differs from
+    the reference's f32 value by at most the metadata rounding."""
+    import torch
+    rng = np.random.default_rng(14)
+    L, H, D, bs, N, T = 1, 8, 128, 16, 8, 64
+    k = rand_rows(rng, (L, T, H, D), orc.BF16, 0.01)
+    slots = np.arange(T, dtype=np.int32)
+    outs = {}
+    for meta in (orc.F32, orc.F16):
+        pool = rmlx_kv.KVPool(L, H, D, bs, N, dtype=orc.BF16, quant_bits=8, group_size=64,
+                              meta_dtype=meta)
+        pool.append(to_dev(k), to_dev(k), to_dev(slots), T)
+        bt = np.arange(4, dtype=np.int32).reshape(1, 4)
+        o = torch.empty(T * H * D, dtype=torch.int16, device=cuda)
+        pool.gather(0, to_dev(bt), 4, to_dev(np.array([T], np.int32)), 1, o, torch.empty_like(o))
+        outs[meta] = orc.dtype_to_f32(to_host(o, np.uint16), orc.BF16)
+        pool.close()
+    x = orc.dtype_to_f32(k, orc.BF16).reshape(T, H, D).transpose(1, 0, 2).reshape(-1)
+    err32 = np.abs(outs[orc.F32] - x).max()
+    err16 = np.abs(outs[orc.F16] - x).max()
+    # 8-bit: |error| <= scale/2 + bf16 rounding; scale <= (range)/255 with range ~ <= 2*8*4.5
+    assert err32 < 0.25 and err16 < 0.3
