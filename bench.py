@@ -55,16 +55,22 @@ def measured_peak():
         return 6650.0, "fallback"
 
 
-def profile_traffic(name):
-    """Per-launch DRAM bytes of `name` from its committed ncu summary, if any."""
+def profile_traffic(name, algorithmic_bytes):
+    """DRAM bytes (read + write) per launch from the kernel's committed ncu
+    summary, scaled from the captured launch to this launch by algorithmic
+    bytes (the traffic of a gather grows in proportion to the rows moved)."""
     p = os.path.join(ROOT, "profiles", name)
+    vals = {}
     try:
         for line in open(p):
-            if line.startswith("traffic_bytes_per_launch:"):
-                return float(line.split(":")[1])
+            if line.startswith("traffic_"):
+                k, v = line.split(":", 1)
+                vals[k.strip()] = float(v)
     except OSError:
-        pass
-    return None
+        return None
+    if "traffic_bytes_per_launch" not in vals or "traffic_algorithmic_bytes" not in vals:
+        return None
+    return round(vals["traffic_bytes_per_launch"] / vals["traffic_algorithmic_bytes"] * algorithmic_bytes)
 
 
 def make_workload(steps_total, heads_local):
@@ -224,14 +230,19 @@ def run_reference(args, rank, world):
 
 
 def main():
+    global LAYERS
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=LAYERS,
+                    help="layers in the pool (profiling runs only; a gather moves the same bytes per layer)")
+    ap.add_argument("--quick", action="store_true", help="device-timed loop only (profiling runs)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    LAYERS = args.layers
 
     rank, world, local = env_int("RANK", 0), env_int("WORLD_SIZE", 1), env_int("LOCAL_RANK", 0)
     if args.impl == "reference":
@@ -341,6 +352,16 @@ def main():
     value = tot_bytes / (elapsed_ms * 1e-3) / 1e9
     ms_per_step = elapsed_ms / K
 
+    if args.quick:
+        if rank == 0:
+            print(json.dumps({"quick": True, "layers": LAYERS, "ms_per_step": round(ms_per_step, 4),
+                              "value": round(value, 2), "gather_launch_ms": round(float(np.mean(gather_ms)), 4)}))
+        clocks.stop()
+        pool.close()
+        if dist is not None:
+            dist.destroy_process_group()
+        return
+
     # ---- e2e: the same steps through the public API with host buffers ----
     # Per step: block-manager allocation for sequences crossing a block
     # boundary, H2D of the new K/V (pinned), slots, block tables and lengths,
@@ -405,7 +426,7 @@ def main():
     g_bytes = float(np.mean(gather_bytes))
     g_ms = float(np.mean(gather_ms))
     achieved = g_bytes / (g_ms * 1e-3) / 1e9
-    traffic = profile_traffic("gather_rows_kernel_llama8b_decode.txt")
+    traffic = profile_traffic("gather_rows_kernel_llama8b_decode.txt", g_bytes)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

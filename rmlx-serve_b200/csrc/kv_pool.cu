@@ -138,16 +138,47 @@ __device__ __forceinline__ int find_seq(const int32_t* cub, int n, int64_t gi) {
 }
 
 // ---------------------------------------------------------------------------
-// Gather (plain): persistent CTAs; one warp per (sequence block, kv, head)
-// tile.  Units are ordered with the head fastest so that consecutive warps
-// read the adjacent head tiles of one pool block; each full tile lands as
-// one contiguous block_size * row_bytes run in the [seq][head][len][dim]
-// output.
+// Gather (plain): persistent CTAs, two CTAs of 256 threads per SM; each warp
+// copies two (sequence block, kv, head) tiles per round with all 16 loads
+// of a lane in flight before its stores.  Units are ordered with the head
+// fastest so that a warp's two tiles (and its neighbours') are adjacent head
+// tiles of one pool block; each full tile lands as one contiguous
+// block_size * row_bytes run in the [seq][head][len][dim] output.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) gather_rows_kernel(PoolGeo g, int layer, const int32_t* __restrict__ bt,
-                                                          int bt_stride, const int32_t* __restrict__ lens, int nseq,
-                                                          uint8_t* __restrict__ ok, uint8_t* __restrict__ ov,
-                                                          int32_t* err) {
+struct TileRef {
+  const uint8_t* src;
+  uint8_t* dst;
+  int n16;
+};
+
+__device__ __forceinline__ TileRef gather_tile(const PoolGeo& g, int layer, int64_t u, int64_t units,
+                                               const int32_t* __restrict__ bt, int bt_stride, const int32_t* cub,
+                                               const int32_t* cut, int nseq, uint8_t* ok, uint8_t* ov,
+                                               int64_t out_row_bytes, int lane, int32_t* err) {
+  TileRef t{nullptr, nullptr, 0};
+  if (u >= units) return t;
+  const int h = (int)(u % g.heads);
+  const int64_t q = u / g.heads;
+  const int kv = (int)(q & 1);
+  const int64_t gi = q >> 1;
+  const int s = find_seq(cub, nseq, gi);
+  const int b = (int)(gi - cub[s]);
+  const int L = cut[s + 1] - cut[s];
+  const int32_t blk = __ldg(bt + (int64_t)s * bt_stride + b);
+  if (blk < 0 || blk >= g.nblocks) {
+    if (lane == 0) atomicOr(err, DEV_ERR_BLOCK);
+    return t;
+  }
+  t.src = g.base + g.tile_off(blk, layer, kv, h);
+  t.dst = (kv ? ov : ok) + ((int64_t)cut[s] * g.heads + (int64_t)h * L + (int64_t)b * g.bs) * out_row_bytes;
+  t.n16 = min(g.bs, L - b * g.bs) * g.row_bytes / 16;
+  return t;
+}
+
+__global__ void __launch_bounds__(256, 2) gather_rows_kernel(PoolGeo g, int layer, const int32_t* __restrict__ bt,
+                                                             int bt_stride, const int32_t* __restrict__ lens,
+                                                             int nseq, uint8_t* __restrict__ ok,
+                                                             uint8_t* __restrict__ ov, int32_t* err) {
   extern __shared__ int32_t smem[];
   int32_t* cub = smem;
   int32_t* cut = smem + nseq + 1;
@@ -155,23 +186,10 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(PoolGeo g, int layer, 
   const int64_t units = (int64_t)cub[nseq] * 2 * g.heads;
   const int lane = threadIdx.x & 31;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  for (int64_t u = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; u < units; u += nwarps) {
-    int h = (int)(u % g.heads);
-    int64_t q = u / g.heads;
-    int kv = (int)(q & 1);
-    int64_t gi = q >> 1;
-    int s = find_seq(cub, nseq, gi);
-    int b = (int)(gi - cub[s]);
-    int L = cut[s + 1] - cut[s];
-    int nrows = min(g.bs, L - b * g.bs);
-    int32_t blk = __ldg(bt + (int64_t)s * bt_stride + b);
-    if (blk < 0 || blk >= g.nblocks) {
-      if (lane == 0) atomicOr(err, DEV_ERR_BLOCK);
-      continue;
-    }
-    const uint8_t* src = g.base + g.tile_off(blk, layer, kv, h);
-    uint8_t* dst = (kv ? ov : ok) + ((int64_t)cut[s] * g.heads + (int64_t)h * L + (int64_t)b * g.bs) * g.row_bytes;
-    warp_copy(src, dst, nrows * g.row_bytes / 16, lane);
+  for (int64_t u = ((blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5) * 2; u < units; u += nwarps * 2) {
+    const TileRef a = gather_tile(g, layer, u, units, bt, bt_stride, cub, cut, nseq, ok, ov, g.row_bytes, lane, err);
+    const TileRef b = gather_tile(g, layer, u + 1, units, bt, bt_stride, cub, cut, nseq, ok, ov, g.row_bytes, lane, err);
+    warp_copy2(a.src, a.dst, a.n16, b.src, b.dst, b.n16, lane);
   }
 }
 
@@ -434,42 +452,51 @@ __global__ void __launch_bounds__(256) gather_dequant_kernel(PoolGeo g, int laye
 }
 
 // ---------------------------------------------------------------------------
-// Block copy / pack / unpack: one warp per 4 KiB segment of a block.
+// Block copy / pack / unpack: a warp copies two 4 KiB segments per round.
 //   mode 0: pool[dst[i]] = pool[src[i]]
 //   mode 1: staging[i]   = pool[src[i]]       (pack)
 //   mode 2: pool[src[i]] = staging[i]         (unpack)
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) copy_blocks_kernel(uint8_t* base, int64_t block_bytes, int nblocks,
-                                                          const int32_t* __restrict__ src,
-                                                          const int32_t* __restrict__ dst, int n, int mode,
-                                                          uint8_t* staging, int32_t* err) {
+__device__ __forceinline__ TileRef copy_segment(uint8_t* base, int64_t block_bytes, int nblocks,
+                                                const int32_t* __restrict__ src, const int32_t* __restrict__ dst,
+                                                int64_t u, int64_t units, int64_t segs, int mode, uint8_t* staging,
+                                                int lane, int32_t* err) {
+  TileRef t{nullptr, nullptr, 0};
+  if (u >= units) return t;
+  const int i = (int)(u / segs);
+  const int64_t off = (u - (int64_t)i * segs) * 4096;
+  const int32_t a = __ldg(src + i);
+  const int32_t b = mode == 0 ? __ldg(dst + i) : 0;
+  if (a < 0 || a >= nblocks || b < 0 || b >= nblocks) {
+    if (lane == 0 && off == 0) atomicOr(err, DEV_ERR_BLOCK);
+    return t;
+  }
+  if (mode == 0) {
+    t.src = base + (int64_t)a * block_bytes + off;
+    t.dst = base + (int64_t)b * block_bytes + off;
+  } else if (mode == 1) {
+    t.src = base + (int64_t)a * block_bytes + off;
+    t.dst = staging + (int64_t)i * block_bytes + off;
+  } else {
+    t.src = staging + (int64_t)i * block_bytes + off;
+    t.dst = base + (int64_t)a * block_bytes + off;
+  }
+  t.n16 = (int)(min((int64_t)4096, block_bytes - off) / 16);
+  return t;
+}
+
+__global__ void __launch_bounds__(256, 2) copy_blocks_kernel(uint8_t* base, int64_t block_bytes, int nblocks,
+                                                             const int32_t* __restrict__ src,
+                                                             const int32_t* __restrict__ dst, int n, int mode,
+                                                             uint8_t* staging, int32_t* err) {
   const int64_t segs = (block_bytes + 4095) / 4096;
   const int64_t units = (int64_t)n * segs;
   const int lane = threadIdx.x & 31;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  for (int64_t u = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; u < units; u += nwarps) {
-    const int i = (int)(u / segs);
-    const int64_t off = (u - (int64_t)i * segs) * 4096;
-    const int bytes = (int)min((int64_t)4096, block_bytes - off);
-    const int32_t a = __ldg(src + i);
-    const int32_t b = mode == 0 ? __ldg(dst + i) : 0;
-    if (a < 0 || a >= nblocks || b < 0 || b >= nblocks) {
-      if (lane == 0) atomicOr(err, DEV_ERR_BLOCK);
-      continue;
-    }
-    const uint8_t* sp;
-    uint8_t* dp;
-    if (mode == 0) {
-      sp = base + (int64_t)a * block_bytes + off;
-      dp = base + (int64_t)b * block_bytes + off;
-    } else if (mode == 1) {
-      sp = base + (int64_t)a * block_bytes + off;
-      dp = staging + (int64_t)i * block_bytes + off;
-    } else {
-      sp = staging + (int64_t)i * block_bytes + off;
-      dp = base + (int64_t)a * block_bytes + off;
-    }
-    warp_copy(sp, dp, bytes / 16, lane);
+  for (int64_t u = ((blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5) * 2; u < units; u += nwarps * 2) {
+    const TileRef a = copy_segment(base, block_bytes, nblocks, src, dst, u, units, segs, mode, staging, lane, err);
+    const TileRef b = copy_segment(base, block_bytes, nblocks, src, dst, u + 1, units, segs, mode, staging, lane, err);
+    warp_copy2(a.src, a.dst, a.n16, b.src, b.dst, b.n16, lane);
   }
 }
 
@@ -738,7 +765,7 @@ static rmlx_status launch_copy(rmlx_kv_pool* p, const int32_t* a, const int32_t*
   if (mode != 0 && !aligned16(staging)) return fail(RMLX_E_BAD_ARG, "staging must be 16-byte aligned");
   DeviceGuard dg(p->device);
   const int64_t units = (int64_t)n * (((int64_t)p->block_bytes + 4095) / 4096);
-  const int grid = (int)std::min<int64_t>((units + 7) / 8, (int64_t)p->num_sms * 8);
+  const int grid = (int)std::min<int64_t>((units + 15) / 16, (int64_t)p->num_sms * 2);
   copy_blocks_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(p->base, (int64_t)p->block_bytes, p->cfg.num_blocks, a,
                                                              b, n, mode, staging, p->err);
   return cuda_check(cudaGetLastError(), "copy_blocks launch");
