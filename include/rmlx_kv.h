@@ -206,6 +206,24 @@ RMLX_API size_t rmlx_qcache_group_size(const rmlx_qcache* q);
 RMLX_API rmlx_status rmlx_qcache_raw(rmlx_qcache* q, size_t layer, int32_t which, uint8_t* bytes, size_t bytes_cap,
                             float* scales, float* zeros, size_t groups_cap, size_t* n_bytes, size_t* n_groups);
 
+/* Same values as rmlx_qcache_get_keys_dequantized (which = 0) or
+ * rmlx_qcache_get_values_dequantized (which = 1), but allocating nothing: the
+ * values pass through a fixed device array of RMLX_QCACHE_STATIC_MAX_FLOATS
+ * floats (8 MiB) that the library holds on every GPU it is loaded on, until
+ * the process exits.  No counterpart in the reference (its cache lives in
+ * host memory).  It is for callers that must not call cudaMalloc while they
+ * run: an engine that gave nearly all free GPU memory to its KV pool at
+ * start-up, where a later allocation can fail or take memory promised to the
+ * pool, and per-step code that cannot afford the device-wide synchronisation
+ * an allocation may cause.  A layer with more values than the array holds is
+ * refused with RMLX_E_BAD_ARG (out = NULL, cap = 0 still reports *n_out).  The
+ * first call on a device looks up the array's device address; make that first
+ * call before any stream capture.  All calls share the array: calls whose work
+ * overlaps on the same GPU race. */
+#define RMLX_QCACHE_STATIC_MAX_FLOATS ((size_t)2 * 1024 * 1024)
+RMLX_API rmlx_status rmlx_qcache_get_dequantized_static(rmlx_qcache* q, size_t layer, int32_t which, float* out,
+                                                        size_t cap, size_t* n_out);
+
 /* ======================================================================
  * Paged KV pool on one GPU (device data plane).
  *

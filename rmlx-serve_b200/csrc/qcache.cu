@@ -10,6 +10,7 @@
 // dequantize_data (:200-223) including its reading frame: group g reads
 // bytes [g * bytes_per_group, ...) whatever the appends stored, and a group
 // that starts past the end is the reference's slice panic (RMLX_E_BAD_ARG).
+#include <mutex>
 #include <new>
 #include <vector>
 
@@ -190,6 +191,83 @@ rmlx_status dequantize_layer(rmlx_qcache* q, QLayer& L, float* out, size_t cap, 
 }
 
 }  // namespace
+
+// ---------------------------------------------------------------------------
+// Dequantise through a fixed device array instead of allocated scratch.
+//
+// Some callers cannot call cudaMalloc while they run: a serving engine that
+// gave nearly all free GPU memory to its KV pool at start-up (rmlx-serve's
+// CacheConfig defaults gpu_memory_utilization to 0.9) may see a later
+// allocation fail or eat into memory it already promised the pool, and code
+// on the per-step path cannot afford the device-wide synchronisation that
+// cudaMalloc/cudaFree may cause.  rmlx_qcache_get_dequantized_static serves
+// them: it stages the dequantised values in g_static_dequant, a file-scope
+// device array that exists on every GPU that loads this library, for as long
+// as the process runs, and it calls no allocator.
+//
+// In host code `g_static_dequant` names a host-side stand-in, not device
+// memory, so the device address is looked up once per device (with that
+// device current) and cached in g_static_addr.  Every call shares the one
+// array per device and leaves its values there; the kernel overwrites every
+// value a call copies out, so nothing needs clearing between calls, but two
+// calls whose work overlaps on the same GPU race on the array.
+// ---------------------------------------------------------------------------
+static constexpr size_t kStaticMaxFloats = RMLX_QCACHE_STATIC_MAX_FLOATS;
+static __device__ __align__(256) float g_static_dequant[kStaticMaxFloats];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_static_mu;
+float* g_static_addr[kMaxDevices] = {};
+
+// Device address of g_static_dequant on `device` (already current).
+rmlx_status static_scratch(int device, float** out) {
+  if (device < 0 || device >= kMaxDevices) return fail(RMLX_E_BAD_ARG, "device %d out of range", device);
+  std::lock_guard<std::mutex> lk(g_static_mu);
+  if (!g_static_addr[device]) {
+    void* p = nullptr;
+    rmlx_status s = cuda_check(cudaGetSymbolAddress(&p, g_static_dequant), "cudaGetSymbolAddress(static scratch)");
+    if (s != RMLX_OK) return s;
+    g_static_addr[device] = static_cast<float*>(p);
+  }
+  *out = g_static_addr[device];
+  return RMLX_OK;
+}
+}  // namespace
+
+extern "C" rmlx_status rmlx_qcache_get_dequantized_static(rmlx_qcache* q, size_t layer, int32_t which, float* out,
+                                                          size_t cap, size_t* n_out) {
+  if (!q || !n_out) return fail(RMLX_E_BAD_ARG, "NULL cache or n_out");
+  if (layer >= q->layers) return fail(RMLX_E_RANGE, "layer %zu out of range", layer);
+  if (which != 0 && which != 1) return fail(RMLX_E_BAD_ARG, "which must be 0 (keys) or 1 (values)");
+  QLayer& L = which ? q->v[layer] : q->k[layer];
+  *n_out = 0;
+  if (L.bytes.len == 0 || L.scales.len == 0) return RMLX_OK;
+  const size_t bpg = q->bits == 4 ? (q->gs + 1) / 2 : q->gs;
+  const size_t vpb = q->bits == 4 ? 2 : 1;
+  const size_t ng = L.scales.len;
+  if ((ng - 1) * bpg > L.bytes.len)
+    return fail(RMLX_E_BAD_ARG, "group %zu starts past the %zu stored bytes (slice out of range)", ng - 1, L.bytes.len);
+  const size_t n = ((ng - 1) * bpg + std::min(bpg, L.bytes.len - (ng - 1) * bpg)) * vpb;
+  *n_out = n;
+  if (!out) return RMLX_OK;
+  if (n > kStaticMaxFloats)
+    return fail(RMLX_E_BAD_ARG, "%zu values exceed the static scratch of %zu floats", n, kStaticMaxFloats);
+  if (cap < n) return fail(RMLX_E_BAD_ARG, "output holds %zu floats, %zu needed", cap, n);
+  DeviceGuard dg(q->device);
+  float* scratch = nullptr;
+  rmlx_status s = static_scratch(q->device, &scratch);
+  if (s != RMLX_OK) return s;
+  const int grid = (int)((ng * 32 + 255) / 256);
+  if (q->bits == 8)
+    qcache_dequant_kernel<8><<<grid, 256>>>(L.bytes.ptr, (int64_t)L.bytes.len, (int)bpg, (int)ng, L.scales.ptr,
+                                            L.zeros.ptr, scratch);
+  else
+    qcache_dequant_kernel<4><<<grid, 256>>>(L.bytes.ptr, (int64_t)L.bytes.len, (int)bpg, (int)ng, L.scales.ptr,
+                                            L.zeros.ptr, scratch);
+  if ((s = cuda_check(cudaGetLastError(), "static dequant launch")) != RMLX_OK) return s;
+  return cuda_check(cudaMemcpy(out, scratch, n * sizeof(float), cudaMemcpyDeviceToHost), "static dequant copy-out");
+}
 
 extern "C" {
 
