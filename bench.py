@@ -1,20 +1,27 @@
 #!/usr/bin/env python3
-"""Decode-step KV-cache benchmark (paged append + per-layer paged gather).
+"""KV-cache step benchmark: paged append + per-layer paged gather.
 
-Workload: Llama-3.1-8B KV shape -- 32 layers, 8 KV heads, head_dim 128,
-block 16, bf16; batch 64, context lengths uniform in [512, 4096]; every step
-appends one token per sequence to every layer, then gathers every layer's
-K/V for all sequences through the block tables.  Block tables are drawn
-from a seeded permutation of a pool sized 1.25x the blocks in use.
+Default workload (``--workload decode``): Llama-3.1-8B KV shape -- 32
+layers, 8 KV heads, head_dim 128, block 16, bf16; batch 64, context lengths
+uniform in [512, 4096]; every step appends one token per sequence to every
+layer, then gathers every layer's K/V for all sequences through the block
+tables.  Block tables are drawn from a seeded permutation of a pool sized
+1.25x the blocks in use.
+
+``--workload quant8`` / ``quant4``: the same layers and heads, batch 128,
+contexts uniform in [1024, 8192], K/V N(0,1) with 1% outliers x8, stored as
+8-bit / 4-bit group-affine codes (group 64 along head_dim, fp16 scale and
+zero per group): quantise-on-append, dequantise-on-gather to bf16.
 
 With N GPUs (one process per GPU under torchrun) the 8 KV heads are split
 over the GPUs: each rank owns 8/N heads of every block and runs the same
 step on them; there is no collective in the step.
 
-Metric: algorithmic HBM GB/s of the step (K/V bytes read + written by the
-append and the gathers), whole job; also microseconds per decode step.
+Metric: algorithmic HBM GB/s of the step (bytes the append and the gathers
+must read and write), whole job; also microseconds per step.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+                  [--workload decode|quant8|quant4]
 """
 import argparse
 import json
@@ -24,19 +31,71 @@ import subprocess
 import sys
 import tempfile
 import time
+from dataclasses import dataclass
 
 import numpy as np
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "rmlx-serve_b200"))
 
-LAYERS, HEADS, HEAD_DIM, BLOCK, BATCH = 32, 8, 128, 16, 64
-CTX_LO, CTX_HI = 512, 4096
-ESIZE = 2  # bf16
-SEED = 0x5EED + 2
-METRIC = "KV append+gather HBM GB/s (decode step, Llama-3.1-8B KV shape)"
-WORKLOAD = ("decode-step KV ops: 32 layers x 8 KV heads x 128, block 16, bf16, batch 64, "
-            "ctx U[512,4096], append 1 token/seq/layer then paged gather of every layer")
+F32, F16, BF16 = 0, 1, 2
+
+
+@dataclass
+class Workload:
+    name: str
+    metric: str
+    desc: str
+    seed: int
+    layers: int = 32
+    heads: int = 8
+    head_dim: int = 128
+    block: int = 16
+    batch: int = 64
+    ctx_lo: int = 512
+    ctx_hi: int = 4096
+    bits: int = 0
+    group: int = 64
+    meta: int = F16
+    outliers: float = 0.0
+
+    # bytes of one token's rows of the local heads
+    def in_row(self, h):
+        return h * self.head_dim * 2
+
+    def stored_row(self, h):
+        return h * self.head_dim * self.bits // 8 if self.bits else self.in_row(h)
+
+    def meta_row(self, h):
+        return h * (self.head_dim // self.group) * 2 * (2 if self.meta == F16 else 4) if self.bits else 0
+
+    @property
+    def kernel(self):
+        return "gather_dequant_kernel" if self.bits else "gather_rows_kernel"
+
+    @property
+    def profile(self):
+        return f"{self.kernel}_llama8b_{self.name}.txt"
+
+
+WORKLOADS = {
+    "decode": Workload(
+        "decode", "KV append+gather HBM GB/s (decode step, Llama-3.1-8B KV shape)",
+        "decode-step KV ops: 32 layers x 8 KV heads x 128, block 16, bf16, batch 64, ctx U[512,4096], "
+        "append 1 token/seq/layer then paged gather of every layer", seed=0x5EED + 2),
+    "quant8": Workload(
+        "quant8", "KV quant-append + dequant-gather HBM GB/s (8-bit, Llama-3.1-8B KV shape)",
+        "quantised KV store: 32 layers x 8 KV heads x 128, block 16, 8-bit codes, group 64, fp16 scale/zero, "
+        "batch 128, ctx U[1024,8192], 1% outliers x8; quantise-on-append 1 token/seq/layer, then "
+        "dequantise-on-gather (bf16) of every layer", seed=0x5EED + 3, batch=128, ctx_lo=1024, ctx_hi=8192, bits=8,
+        outliers=0.01),
+    "quant4": Workload(
+        "quant4", "KV quant-append + dequant-gather HBM GB/s (4-bit, Llama-3.1-8B KV shape)",
+        "quantised KV store: 32 layers x 8 KV heads x 128, block 16, 4-bit codes (2 per byte), group 64, fp16 "
+        "scale/zero, batch 128, ctx U[1024,8192], 1% outliers x8; quantise-on-append 1 token/seq/layer, then "
+        "dequantise-on-gather (bf16) of every layer", seed=0x5EED + 3, batch=128, ctx_lo=1024, ctx_hi=8192, bits=4,
+        outliers=0.01),
+}
 
 
 def env_int(name, default):
@@ -47,9 +106,8 @@ def env_int(name, default):
 
 
 def measured_peak():
-    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
-        with open(p) as f:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             return float(json.load(f)["hbm_gbs"]), "measured"
     except Exception:
         return 6650.0, "fallback"
@@ -59,10 +117,9 @@ def profile_traffic(name, algorithmic_bytes):
     """DRAM bytes (read + write) per launch from the kernel's committed ncu
     summary, scaled from the captured launch to this launch by algorithmic
     bytes (the traffic of a gather grows in proportion to the rows moved)."""
-    p = os.path.join(ROOT, "profiles", name)
     vals = {}
     try:
-        for line in open(p):
+        for line in open(os.path.join(ROOT, "profiles", name)):
             if line.startswith("traffic_"):
                 k, v = line.split(":", 1)
                 vals[k.strip()] = float(v)
@@ -73,46 +130,45 @@ def profile_traffic(name, algorithmic_bytes):
     return round(vals["traffic_bytes_per_launch"] / vals["traffic_algorithmic_bytes"] * algorithmic_bytes)
 
 
-def make_workload(steps_total, heads_local):
+def make_workload(w, steps_total):
     """Seeded lengths, block tables (through the product's block manager) and
-    per-step slot mappings for `steps_total` decode steps."""
+    per-step slot mappings for `steps_total` steps."""
     import rmlx_kv
-    rng = np.random.default_rng(SEED)
-    lens0 = rng.integers(CTX_LO, CTX_HI + 1, size=BATCH).astype(np.int64)
-    final = lens0 + steps_total
-    need = (final + BLOCK - 1) // BLOCK
+    rng = np.random.default_rng(w.seed)
+    lens0 = rng.integers(w.ctx_lo, w.ctx_hi + 1, size=w.batch).astype(np.int64)
+    need = (lens0 + steps_total + w.block - 1) // w.block
     num_blocks = int(np.ceil(1.25 * need.sum()))
-    mgr = rmlx_kv.PagedCacheManager(BLOCK, num_blocks)
+    mgr = rmlx_kv.PagedCacheManager(w.block, num_blocks)
     # Make the free list a seeded permutation of the pool: allocate all, free
     # in permuted order (FIFO reuse hands them out in that order).
-    allb = mgr.allocate_n(num_blocks)
-    mgr.free_n(rng.permutation(allb))
-    width = int(need.max())
-    bt = np.zeros((BATCH, width), dtype=np.int32)
-    nblk = np.zeros(BATCH, dtype=np.int64)
-    for s in range(BATCH):
-        n0 = (int(lens0[s]) + BLOCK - 1) // BLOCK
+    mgr.free_n(rng.permutation(mgr.allocate_n(num_blocks)))
+    bt = np.zeros((w.batch, int(need.max())), dtype=np.int32)
+    nblk = np.zeros(w.batch, dtype=np.int64)
+    for s in range(w.batch):
+        n0 = (int(lens0[s]) + w.block - 1) // w.block
         bt[s, :n0] = mgr.allocate_n(n0)
         nblk[s] = n0
-    slots = np.zeros((steps_total, BATCH), dtype=np.int32)
+    slots = np.zeros((steps_total, w.batch), dtype=np.int32)
     for st in range(steps_total):
-        for s in range(BATCH):
+        for s in range(w.batch):
             p = int(lens0[s]) + st
-            while p // BLOCK >= nblk[s]:
+            while p // w.block >= nblk[s]:
                 bt[s, nblk[s]] = mgr.allocate_n(1)[0]
                 nblk[s] += 1
-            slots[st, s] = bt[s, p // BLOCK] * BLOCK + p % BLOCK
-    return dict(lens0=lens0, bt=bt, slots=slots, num_blocks=num_blocks, mgr=mgr, rng=rng)
+            slots[st, s] = bt[s, p // w.block] * w.block + p % w.block
+    return dict(lens0=lens0, bt=bt, slots=slots, num_blocks=num_blocks, mgr=mgr)
 
 
-def step_bytes(lens, heads):
-    """Algorithmic bytes of one step: append (read new rows + write them) and
-    a gather of every layer (read rows + write rows, K and V), plus the
-    block-table entries and lengths the gathers read."""
-    row = heads * HEAD_DIM * ESIZE
-    append = 2 * 2 * BATCH * LAYERS * row
-    blocks = int(((lens + BLOCK - 1) // BLOCK).sum())
-    gather_one = 2 * 2 * int(lens.sum()) * row + 4 * blocks + 4 * BATCH
+def step_bytes(w, lens, heads, layers=None):
+    """Algorithmic bytes of one step.  Append: read every new row, write its
+    stored form (and its scale/zero).  Gather of one layer: read every stored
+    row (and meta) of every sequence, write it out in the input type; plus
+    the block-table entries and lengths the gather reads.  K and V both."""
+    layers = w.layers if layers is None else layers
+    i, s, m = w.in_row(heads), w.stored_row(heads), w.meta_row(heads)
+    append = 2 * w.batch * layers * (i + s + m)
+    blocks = int(((lens + w.block - 1) // w.block).sum())
+    gather_one = 2 * int(lens.sum()) * (s + m + i) + 4 * blocks + 4 * w.batch
     return append, gather_one
 
 
@@ -170,83 +226,108 @@ class Clocks:
                 if v.lower().startswith("active"):
                     reasons.add(n)
         os.unlink(self.path)
+        self.proc = None
         if not sm:
             return None
         return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons),
                 "samples": len(sm)}
 
 
-def cpu_sample(steps, warm, threads, lens0, bt, slots, num_blocks):
-    """The oracle (CPU restatement of the reference's row copies) on the host
-    cores: one layer of every step -- append 1 token per sequence, then the
-    full gather of that layer.  Returns (GB/s, seconds per sampled step)."""
+def cpu_sample(w, steps, warm, threads, lens0, bt, slots, num_blocks):
+    """The oracle (CPU restatement of the reference) on the host cores: one
+    layer of every step -- append 1 token per sequence (quantising it for the
+    quantised workloads), then the full gather (dequantise) of that layer,
+    sequences split over `threads`.  Returns (GB/s, seconds per sample)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as orc
-    g = orc.Geo(1, HEADS, HEAD_DIM, BLOCK, num_blocks, ESIZE)
-    pool = np.zeros(g.pool_bytes(), dtype=np.uint8)
-    rng = np.random.default_rng(SEED + 1)
-    pool[:] = rng.integers(0, 256, size=pool.size, dtype=np.uint8)
-    lens_max = lens0 + slots.shape[0]
-    tot = int(lens_max.sum()) * HEADS * HEAD_DIM
+    H, D = w.heads, w.head_dim
+    g = orc.Geo(1, H, D, w.block, num_blocks, 2, bits=w.bits, group_size=w.group,
+                meta_bytes=2 if w.meta == F16 else 4)
+    rng = np.random.default_rng(w.seed + 1)
+    pool = rng.integers(0, 256, size=g.pool_bytes(), dtype=np.uint8)
+    if w.bits:
+        # sane scale/zero so that the CPU does not run on random subnormals
+        tb = g.tile_bytes()
+        rb, mrb = D * w.bits // 8, (D // w.group) * 2 * (2 if w.meta == F16 else 4)
+        tiles = pool.reshape(-1, tb)
+        meta = np.tile(np.array([0.02, -2.5], dtype=np.float16 if w.meta == F16 else np.float32),
+                       (tiles.shape[0], w.block * (D // w.group)))
+        tiles[:, w.block * rb:w.block * rb + w.block * mrb] = meta.view(np.uint8)
+    tot = int((lens0 + slots.shape[0]).sum()) * H * D
     ok = np.empty(tot, dtype=np.uint16)
     ov = np.empty(tot, dtype=np.uint16)
-    kin = orc.f32_to_dtype(rng.standard_normal((BATCH, HEADS, HEAD_DIM), dtype=np.float32), orc.BF16)
+    kin = orc.f32_to_dtype(rng.standard_normal((w.batch, H, D), dtype=np.float32), orc.BF16)
     total_bytes, t_total = 0, 0.0
     for st in range(warm + steps):
         lens = (lens0 + st + 1).astype(np.int32)
+        sl = slots[st].astype(np.int64)
         t0 = time.perf_counter()
-        orc.paged_append(pool, g, 0, 1, kin, kin, 0, HEADS * HEAD_DIM, HEAD_DIM, slots[st].astype(np.int64))
-        orc.paged_gather(pool, g, 0, bt, bt.shape[1], lens, ok, ov, threads=threads)
+        if w.bits:
+            orc.paged_append_quant(pool, g, 0, 1, kin, kin, orc.BF16, 0, H * D, D, sl)
+            orc.paged_gather_dequant(pool, g, 0, bt, bt.shape[1], lens, ok, ov, orc.BF16, threads=threads)
+        else:
+            orc.paged_append(pool, g, 0, 1, kin, kin, 0, H * D, D, sl)
+            orc.paged_gather(pool, g, 0, bt, bt.shape[1], lens, ok, ov, threads=threads)
         dt = time.perf_counter() - t0
         if st >= warm:
-            a, gth = step_bytes(lens.astype(np.int64), HEADS)
-            total_bytes += a / LAYERS + gth
+            a, gth = step_bytes(w, lens.astype(np.int64), H, layers=1)
+            total_bytes += a + gth
             t_total += dt
     return total_bytes / t_total / 1e9, t_total / steps
 
 
-def run_reference(args, rank, world):
+def run_reference(args, w, rank, world):
     """--impl reference: the reference's CPU path (the oracle port; the Rust
     reference cannot be built in this image) on all host cores."""
     if rank != 0:
         return
     threads = os.cpu_count() or 1
     steps, warm = max(args.steps // 5, 2), min(args.warmup, 2)
-    w = make_workload(warm + steps, HEADS)
-    gbs, sec = cpu_sample(steps, warm, threads, w["lens0"], w["bt"], w["slots"], w["num_blocks"])
-    ms_full = sec * LAYERS * 1e3  # one sampled layer per step -> a full 32-layer step
-    sample = (f"1 of 32 layers per step (append 1 token/seq + full gather of that layer), batch 64, "
-              f"{steps} timed steps after {warm} warm-up; GB/s is per sampled byte, ms_per_step scaled x32")
+    wl = make_workload(w, warm + steps)
+    gbs, sec = cpu_sample(w, steps, warm, threads, wl["lens0"], wl["bt"], wl["slots"], wl["num_blocks"])
+    sample = (f"1 of {w.layers} layers per step (append 1 token/seq + full gather of that layer), batch {w.batch}, "
+              f"{steps} timed steps after {warm} warm-up; GB/s is per sampled byte, ms_per_step scaled x{w.layers}")
     print(json.dumps({
-        "impl": "reference", "metric": METRIC, "value": round(gbs, 2), "unit": "GB/s", "n_gpus": world,
-        "steps": steps, "warmup": warm, "ms_per_step": round(ms_full, 3), "higher_is_better": True,
+        "impl": "reference", "metric": w.metric, "value": round(gbs, 2), "unit": "GB/s", "n_gpus": world,
+        "steps": steps, "warmup": warm, "ms_per_step": round(sec * w.layers * 1e3, 3), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "batch": BATCH, "layers": LAYERS, "kv_heads": HEADS,
-                   "head_dim": HEAD_DIM, "block_size": BLOCK},
+        "config": config_of(w, w.heads, wl["num_blocks"], 1),
         "cpu_baseline": {"value": round(gbs, 2), "unit": "GB/s", "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": round(gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
 
+def config_of(w, H, num_blocks, world):
+    c = {"workload": w.desc, "batch": w.batch, "layers": w.layers, "kv_heads": w.heads, "kv_heads_per_gpu": H,
+         "head_dim": w.head_dim, "block_size": w.block, "pool_blocks": num_blocks, "sharding": f"kv-head x{world}",
+         "l2": "inputs larger than L2: each gather launch moves >0.1 GB, no flush"}
+    if w.bits:
+        c.update({"quant_bits": w.bits, "group_size": w.group, "meta": "f16" if w.meta == F16 else "f32",
+                  "outliers": w.outliers})
+    return c
+
+
 def main():
-    global LAYERS
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="decode", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--layers", type=int, default=LAYERS,
+    ap.add_argument("--layers", type=int, default=None,
                     help="layers in the pool (profiling runs only; a gather moves the same bytes per layer)")
     ap.add_argument("--quick", action="store_true", help="device-timed loop only (profiling runs)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    LAYERS = args.layers
+    w = WORKLOADS[args.workload]
+    if args.layers:
+        w.layers = args.layers
 
     rank, world, local = env_int("RANK", 0), env_int("WORLD_SIZE", 1), env_int("LOCAL_RANK", 0)
     if args.impl == "reference":
-        return run_reference(args, rank, world)
+        return run_reference(args, w, rank, world)
 
     import torch
     import rmlx_kv
@@ -257,51 +338,70 @@ def main():
         import datetime
         import torch.distributed as dist
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
     else:
         torch.cuda.set_device(0)
     dev = torch.cuda.current_device()
-    if HEADS % world:
-        raise SystemExit(f"{HEADS} KV heads do not split over {world} GPUs")
-    H = HEADS // world
+    if w.heads % world:
+        raise SystemExit(f"{w.heads} KV heads do not split over {world} GPUs")
+    H, D, L, B, BS = w.heads // world, w.head_dim, w.layers, w.batch, w.block
     W, K = args.warmup, args.steps
-    wl = make_workload(W + K, H)
+    wl = make_workload(w, W + K)
     lens0, bt, slots, num_blocks = wl["lens0"], wl["bt"], wl["slots"], wl["num_blocks"]
 
-    pool = rmlx_kv.KVPool(LAYERS, H, HEAD_DIM, BLOCK, num_blocks, dtype=rmlx_kv.BF16, head_offset=rank * H,
-                          device=dev)
-    # K/V ~ N(0,1): fill every block of the pool on the device.
-    gen = torch.Generator(device="cuda").manual_seed(SEED + rank)
-    view = torch.as_tensor(DevView(pool.layout.base, pool.layout.bytes), device="cuda").view(torch.bfloat16)
-    chunk = 1 << 28
-    for o in range(0, view.numel(), chunk):
-        n = min(chunk, view.numel() - o)
-        view[o:o + n].normal_(generator=gen)
-    del view
-
-    stream = torch.cuda.current_stream()
-    sp = stream.cuda_stream
-    kv_shape = (W + K, LAYERS, BATCH, H, HEAD_DIM)
-    new_k = torch.randn(kv_shape, device="cuda", dtype=torch.bfloat16, generator=gen)
-    new_v = torch.randn(kv_shape, device="cuda", dtype=torch.bfloat16, generator=gen)
-    slots_d = torch.from_numpy(slots).cuda()
-    bt_d = torch.from_numpy(bt).cuda()
-    lens_steps = np.stack([(lens0 + s + 1).astype(np.int32) for s in range(W + K)])
-    lens_d = torch.from_numpy(lens_steps).cuda()
-    max_tok = int(lens_steps[-1].sum())
-    out_k = torch.empty(max_tok * H * HEAD_DIM, device="cuda", dtype=torch.bfloat16)
-    out_v = torch.empty_like(out_k)
-    ts, ls = H * HEAD_DIM, BATCH * H * HEAD_DIM
+    pool = rmlx_kv.KVPool(L, H, D, BS, num_blocks, dtype=rmlx_kv.BF16, quant_bits=w.bits, group_size=w.group,
+                          meta_dtype=w.meta, head_offset=rank * H, device=dev)
     h = pool.handle
     lib = _lib.lib
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+    gen = torch.Generator(device="cuda").manual_seed(w.seed + rank)
+
+    def rand_rows(shape):
+        x = torch.randn(shape, device="cuda", dtype=torch.float32, generator=gen)
+        if w.outliers:
+            x = torch.where(torch.rand(shape, device="cuda", generator=gen) < w.outliers, x * 8.0, x)
+        return x.to(torch.bfloat16)
+
+    ts, hs = H * D, D
+    bt_d = torch.from_numpy(bt).cuda()
+    if w.bits:
+        # Prompt K/V ~ N(0,1) (+outliers) quantised into the pool through the
+        # product's own quantise-on-append, a chunk of tokens at a time.
+        pos = [(s, p) for s in range(B) for p in range(int(lens0[s]))]
+        chunk = 4096
+        for o in range(0, len(pos), chunk):
+            part = pos[o:o + chunk]
+            T = len(part)
+            sl = torch.tensor([bt[s, p // BS] * BS + p % BS for s, p in part], dtype=torch.int32, device="cuda")
+            kk, vv = rand_rows((L, T, H, D)), rand_rows((L, T, H, D))
+            _lib.check(lib.rmlx_kv_append(h, 0, L, kk.data_ptr(), vv.data_ptr(), T * ts, ts, hs, sl.data_ptr(), T,
+                                          sp))
+        del kk, vv
+    else:
+        view = torch.as_tensor(DevView(pool.layout.base, pool.layout.bytes), device="cuda").view(torch.bfloat16)
+        step = 1 << 28
+        for o in range(0, view.numel(), step):
+            view[o:o + step].normal_(generator=gen)
+        del view
+
+    kv_shape = (W + K, L, B, H, D)
+    new_k, new_v = rand_rows(kv_shape), rand_rows(kv_shape)
+    slots_d = torch.from_numpy(slots).cuda()
+    lens_steps = np.stack([(lens0 + s + 1).astype(np.int32) for s in range(W + K)])
+    lens_d = torch.from_numpy(lens_steps).cuda()
+    out_k = torch.empty(int(lens_steps[-1].sum()) * H * D, device="cuda", dtype=torch.bfloat16)
+    out_v = torch.empty_like(out_k)
+    ls = B * H * D
 
     def launch_step(s, ev_pairs=None):
-        rc = lib.rmlx_kv_append(h, 0, LAYERS, new_k[s].data_ptr(), new_v[s].data_ptr(), ls, ts, HEAD_DIM,
-                                slots_d[s].data_ptr(), BATCH, sp)
-        for layer in range(LAYERS):
+        rc = lib.rmlx_kv_append(h, 0, L, new_k[s].data_ptr(), new_v[s].data_ptr(), ls, ts, hs,
+                                slots_d[s].data_ptr(), B, sp)
+        for layer in range(L):
             if ev_pairs is not None:
                 ev_pairs[layer][0].record(stream)
-            rc |= lib.rmlx_kv_gather(h, layer, bt_d.data_ptr(), bt.shape[1], lens_d[s].data_ptr(), BATCH,
+            rc |= lib.rmlx_kv_gather(h, layer, bt_d.data_ptr(), bt.shape[1], lens_d[s].data_ptr(), B,
                                      out_k.data_ptr(), out_v.data_ptr(), sp)
             if ev_pairs is not None:
                 ev_pairs[layer][1].record(stream)
@@ -322,11 +422,11 @@ def main():
     for s in range(W):
         rc |= launch_step(s)
     if rc or pool.check() != 0:
-        raise SystemExit("device-side validation error during warm-up")
+        raise SystemExit("launch or device-side validation error during warm-up")
 
     clocks = Clocks(dev)
     clocks.start()
-    ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(LAYERS)]
+    ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(L)]
           for _ in range(K)]
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
@@ -338,25 +438,28 @@ def main():
     torch.cuda.synchronize()
     barrier()
     elapsed_ms = max_over_ranks(e0.elapsed_time(e1))
-    gather_ms = [ev[i][l][0].elapsed_time(ev[i][l][1]) for i in range(K) for l in range(LAYERS)]
+    gather_ms = [ev[i][l][0].elapsed_time(ev[i][l][1]) for i in range(K) for l in range(L)]
     if rc or pool.check() != 0:
         raise SystemExit("launch or device-side validation error in the timed region")
 
     # Algorithmic bytes over the timed steps, all ranks.
     tot_bytes, gather_bytes = 0, []
     for i in range(K):
-        a, g1 = step_bytes(lens_steps[W + i].astype(np.int64), H)
-        tot_bytes += a + LAYERS * g1
-        gather_bytes += [g1] * LAYERS
+        a, g1 = step_bytes(w, lens_steps[W + i].astype(np.int64), H)
+        tot_bytes += a + L * g1
+        gather_bytes += [g1] * L
     tot_bytes *= world
     value = tot_bytes / (elapsed_ms * 1e-3) / 1e9
     ms_per_step = elapsed_ms / K
+    g_bytes = float(np.mean(gather_bytes))
+    g_ms = float(np.mean(gather_ms))
 
     if args.quick:
-        if rank == 0:
-            print(json.dumps({"quick": True, "layers": LAYERS, "ms_per_step": round(ms_per_step, 4),
-                              "value": round(value, 2), "gather_launch_ms": round(float(np.mean(gather_ms)), 4)}))
         clocks.stop()
+        if rank == 0:
+            print(json.dumps({"quick": True, "workload": w.name, "layers": L, "ms_per_step": round(ms_per_step, 4),
+                              "value": round(value, 2), "gather_launch_ms": round(g_ms, 4),
+                              "gather_gbs": round(g_bytes / (g_ms * 1e-3) / 1e9, 1)}))
         pool.close()
         if dist is not None:
             dist.destroy_process_group()
@@ -365,56 +468,53 @@ def main():
     # ---- e2e: the same steps through the public API with host buffers ----
     # Per step: block-manager allocation for sequences crossing a block
     # boundary, H2D of the new K/V (pinned), slots, block tables and lengths,
-    # the append and 32 gathers, and a D2H read of the step's status word.
-    mgr = rmlx_kv.PagedCacheManager(BLOCK, num_blocks)
-    rng = np.random.default_rng(SEED + 7)
+    # the append and the per-layer gathers, and a D2H read of the step's
+    # status word.  The gathered K/V stay in HBM for the attention that
+    # consumes them.
+    mgr = rmlx_kv.PagedCacheManager(BS, num_blocks)
+    rng = np.random.default_rng(w.seed + 7)
     mgr.free_n(rng.permutation(mgr.allocate_n(num_blocks)))
     host_bt = np.zeros_like(bt)
-    nblk = np.zeros(BATCH, dtype=np.int64)
-    for s in range(BATCH):
-        n0 = (int(lens0[s]) + BLOCK - 1) // BLOCK
+    nblk = np.zeros(B, dtype=np.int64)
+    for s in range(B):
+        n0 = (int(lens0[s]) + BS - 1) // BS
         host_bt[s, :n0] = mgr.allocate_n(n0)
         nblk[s] = n0
-    pin_k = torch.empty((K, LAYERS, BATCH, H, HEAD_DIM), dtype=torch.bfloat16, pin_memory=True)
+    pin_k = torch.empty((K, L, B, H, D), dtype=torch.bfloat16, pin_memory=True)
     pin_v = torch.empty_like(pin_k, pin_memory=True)
     pin_k.copy_(new_k[W:W + K].cpu())
     pin_v.copy_(new_v[W:W + K].cpu())
     pin_bt = torch.from_numpy(host_bt).pin_memory()
-    pin_slots = torch.empty(BATCH, dtype=torch.int32, pin_memory=True)
-    pin_lens = torch.empty(BATCH, dtype=torch.int32, pin_memory=True)
-    dk = torch.empty((LAYERS, BATCH, H, HEAD_DIM), device="cuda", dtype=torch.bfloat16)
+    pin_slots = torch.empty(B, dtype=torch.int32, pin_memory=True)
+    pin_lens = torch.empty(B, dtype=torch.int32, pin_memory=True)
+    dk = torch.empty((L, B, H, D), device="cuda", dtype=torch.bfloat16)
     dv = torch.empty_like(dk)
-    d_slots = torch.empty(BATCH, dtype=torch.int32, device="cuda")
-    d_lens = torch.empty(BATCH, dtype=torch.int32, device="cuda")
+    d_slots = torch.empty(B, dtype=torch.int32, device="cuda")
+    d_lens = torch.empty(B, dtype=torch.int32, device="cuda")
     d_bt = torch.empty_like(bt_d)
-    err_word = torch.zeros(1, dtype=torch.int32, pin_memory=True)
-    h2d = 2 * dk.numel() * ESIZE + 2 * BATCH * 4 + host_bt.nbytes
+    h2d = 2 * dk.numel() * 2 + 2 * B * 4 + host_bt.nbytes
     barrier()
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     for i in range(K):
-        lens_np = pin_lens.numpy()
-        sl = pin_slots.numpy()
-        btn = pin_bt.numpy()
-        for s in range(BATCH):
+        lens_np, sl, btn = pin_lens.numpy(), pin_slots.numpy(), pin_bt.numpy()
+        for s in range(B):
             p = int(lens0[s]) + W + i  # position written this step
-            while p // BLOCK >= nblk[s]:
+            while p // BS >= nblk[s]:
                 btn[s, nblk[s]] = mgr.allocate_n(1)[0]
                 nblk[s] += 1
-            sl[s] = btn[s, p // BLOCK] * BLOCK + p % BLOCK
+            sl[s] = btn[s, p // BS] * BS + p % BS
             lens_np[s] = p + 1
         dk.copy_(pin_k[i], non_blocking=True)
         dv.copy_(pin_v[i], non_blocking=True)
         d_slots.copy_(pin_slots, non_blocking=True)
         d_lens.copy_(pin_lens, non_blocking=True)
         d_bt.copy_(pin_bt, non_blocking=True)
-        rc |= lib.rmlx_kv_append(h, 0, LAYERS, dk.data_ptr(), dv.data_ptr(), ls, ts, HEAD_DIM,
-                                 d_slots.data_ptr(), BATCH, sp)
-        for layer in range(LAYERS):
-            rc |= lib.rmlx_kv_gather(h, layer, d_bt.data_ptr(), bt.shape[1], d_lens.data_ptr(), BATCH,
+        rc |= lib.rmlx_kv_append(h, 0, L, dk.data_ptr(), dv.data_ptr(), ls, ts, hs, d_slots.data_ptr(), B, sp)
+        for layer in range(L):
+            rc |= lib.rmlx_kv_gather(h, layer, d_bt.data_ptr(), bt.shape[1], d_lens.data_ptr(), B,
                                      out_k.data_ptr(), out_v.data_ptr(), sp)
-        err_word[0] = pool.check()  # the step's status word, read back to the host
-        if rc or err_word[0]:
+        if rc or pool.check():  # the step's status word, read back to the host
             raise SystemExit("launch or device-side validation error in the e2e loop")
     torch.cuda.synchronize()
     barrier()
@@ -423,39 +523,33 @@ def main():
     e2e_value = tot_bytes / e2e_s / 1e9
 
     peak, peak_kind = measured_peak()
-    g_bytes = float(np.mean(gather_bytes))
-    g_ms = float(np.mean(gather_ms))
     achieved = g_bytes / (g_ms * 1e-3) / 1e9
-    traffic = profile_traffic("gather_rows_kernel_llama8b_decode.txt", g_bytes)
+    traffic = profile_traffic(w.profile, g_bytes)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
-        gbs, _ = cpu_sample(8, 1, threads, lens0, bt[:, :], slots, num_blocks)
+        steps = 8 if not w.bits else 3
+        gbs, _ = cpu_sample(w, steps, 1, threads, lens0, bt, slots, num_blocks)
         cpu = {"value": round(gbs, 2), "unit": "GB/s", "cores": threads, "kind": "port",
-               "sample": "oracle row-copy append+gather, 1 of 32 layers per step, batch 64, 8 timed steps"}
+               "sample": f"oracle append+gather, 1 of {L} layers per step, batch {B}, {steps} timed steps"}
 
     if rank == 0:
-        out = {
-            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": K,
+        print(json.dumps({
+            "metric": w.metric, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": K,
             "warmup": W, "ms_per_step": round(ms_per_step, 4), "us_per_step": round(ms_per_step * 1e3, 1),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic",
-            "config": {"workload": WORKLOAD, "batch": BATCH, "layers": LAYERS, "kv_heads": HEADS,
-                       "kv_heads_per_gpu": H, "head_dim": HEAD_DIM, "block_size": BLOCK,
-                       "pool_blocks": num_blocks, "sharding": f"kv-head x{world}",
-                       "l2": "inputs larger than L2: each gather launch moves ~1.2 GB/N, no flush"},
-            "roofline": {"bound": "hbm", "kernel": "gather_rows_kernel", "achieved": round(achieved, 1),
-                         "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
+            "data": "synthetic", "config": config_of(w, H, num_blocks, world),
+            "roofline": {"bound": "hbm", "kernel": w.kernel, "achieved": round(achieved, 1), "peak": peak,
+                         "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "frac_of_8000_nominal": round(achieved / 8000.0, 4), "traffic": traffic,
                          "algorithmic_bytes_per_launch": int(g_bytes), "launch_ms": round(g_ms, 4)},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": 4, "ms_per_step": round(e2e_s / K * 1e3, 4)},
-            "gpu_launches": K * (1 + LAYERS),
+            "gpu_launches": K * (1 + L),
             "cpu_baseline": cpu,
             "clocks": clk,
-        }
-        print(json.dumps(out), flush=True)
+        }), flush=True)
     pool.close()
     if dist is not None:
         dist.barrier()

@@ -355,98 +355,186 @@ __global__ void __launch_bounds__(256) append_quant_kernel(PoolGeo g, int l0, in
 }
 
 // ---------------------------------------------------------------------------
-// Dequantise-on-gather: persistent CTAs, one warp per tile as in the plain
-// gather.  A lane decodes one 16-byte chunk of codes (16 codes at 8 bits,
-// 32 at 4 bits).  ONE_GROUP: group_size is a multiple of the codes in a
-// chunk, so one (scale, zero) pair serves the whole chunk.
+// Dequantise-on-gather.
+//
+// Per element the reference computes (code as f32) * scale + zero with a
+// rounded multiply then a rounded add (dequantize_group); the kernel keeps
+// exactly that (__fmul_rn, __fadd_rn).  It avoids the slow conversion pipe
+// for the code: a byte permute builds the f32 bit pattern of 2^23 + code
+// (exact for codes < 2^23) and an exact subtraction of 2^23 recovers
+// (float)code.
+//
+// Layout of the work: persistent CTAs, one warp per (sequence block, kv,
+// head) tile.  A lane's task is one 16-byte segment of output (8 bf16/f16
+// or 4 f32 elements) and the code bytes behind it, so consecutive lanes
+// write consecutive 16 bytes (every store instruction covers 512 contiguous
+// bytes) and read consecutive code bytes.  group_size >= 8 and a power of
+// two, so a task never straddles a (scale, zero) group.  All of a round's
+// loads (codes and scale/zero) are issued before its first store.
 // ---------------------------------------------------------------------------
-template <int BITS, int OUT_DT, bool META_F32, bool ONE_GROUP>
-__global__ void __launch_bounds__(256) gather_dequant_kernel(PoolGeo g, int layer, const int32_t* __restrict__ bt,
-                                                             int bt_stride, const int32_t* __restrict__ lens,
-                                                             int nseq, uint8_t* __restrict__ ok,
-                                                             uint8_t* __restrict__ ov, int hd, int gs_log2,
-                                                             int32_t* err) {
-  using E = Elem<OUT_DT>;
-  constexpr int EPC = BITS == 8 ? 16 : 32;  // elements per 16-byte code chunk
-  constexpr int U = 4;                      // chunks per lane in flight
+
+// f32 value of byte `b` of `w`, via the bit pattern of 2^23 + byte.
+__device__ __forceinline__ float code_byte(uint32_t w, int b) {
+  return __fadd_rn(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440u | (uint32_t)b)), -8388608.0f);
+}
+
+template <bool META_F32>
+__device__ __forceinline__ void meta_at(const uint8_t* mrow, int gq, float& sc, float& zr) {
+  if (META_F32) {
+    const float2 m = __ldg(reinterpret_cast<const float2*>(mrow) + gq);
+    sc = m.x;
+    zr = m.y;
+  } else {
+    const float2 m = __half22float2(__ldg(reinterpret_cast<const __half2*>(mrow) + gq));
+    sc = m.x;
+    zr = m.y;
+  }
+}
+
+// Non-coherent loads of the code bytes of one task (2, 4 or 8 bytes).
+template <int CB>
+__device__ __forceinline__ uint2 load_codes(const uint8_t* p) {
+  uint2 r = make_uint2(0u, 0u);
+  if (CB == 8) {
+    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
+  } else if (CB == 4) {
+    asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(r.x) : "l"(p));
+  } else {
+    unsigned short h;
+    asm volatile("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(h) : "l"(p));
+    r.x = h;
+  }
+  return r;
+}
+
+template <int DT>
+struct Store16;  // 16 bytes of output from f32 values, round-to-nearest-even
+template <>
+struct Store16<RMLX_F32> {
+  static constexpr int n = 4;
+  __device__ __forceinline__ static void run(uint8_t* p, const float* f) {
+    st_stream(p, make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]),
+                            __float_as_uint(f[3])));
+  }
+};
+template <>
+struct Store16<RMLX_F16> {
+  static constexpr int n = 8;
+  __device__ __forceinline__ static void run(uint8_t* p, const float* f) { Elem<RMLX_F16>::store8(p, f); }
+};
+template <>
+struct Store16<RMLX_BF16> {
+  static constexpr int n = 8;
+  __device__ __forceinline__ static void run(uint8_t* p, const float* f) { Elem<RMLX_BF16>::store8(p, f); }
+};
+
+// One round of a warp over TPW tiles: tasks base + lane + 32 v (v < V) of
+// each tile.  All loads (codes, scale/zero) are issued before the first store.
+// Task t reads code bytes [t * CB, (t + 1) * CB) (code rows are contiguous)
+// and writes output bytes [16 t, 16 t + 16) (the tile's output rows are
+// contiguous too).
+template <int BITS, int OUT_DT, bool META_F32, bool POW2, int TPW, int V>
+__device__ __forceinline__ void dq_round(const PoolGeo& g, const uint8_t* const* tile, uint8_t* const* out,
+                                         const int* ntasks, int base, int lane, int tpr, int tpr_log2, int gs_log2) {
+  constexpr int EPT = Store16<OUT_DT>::n;  // output elements per task (16 bytes)
+  constexpr int CB = EPT * BITS / 8;       // code bytes per task
+  const int meta_off = g.bs * g.row_bytes;
+  uint2 cw[TPW][V];
+  float sc[TPW][V], zr[TPW][V];
+#pragma unroll
+  for (int k = 0; k < TPW; ++k)
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      const int t = base + lane + 32 * v;
+      cw[k][v] = make_uint2(0u, 0u);
+      sc[k][v] = zr[k][v] = 0.0f;
+      if (t < ntasks[k]) {
+        cw[k][v] = load_codes<CB>(tile[k] + t * CB);
+        const int r = POW2 ? (t >> tpr_log2) : t / tpr;
+        const int e0 = (POW2 ? (t & (tpr - 1)) : (t - r * tpr)) * EPT;
+        meta_at<META_F32>(tile[k] + meta_off + r * g.meta_row_bytes, e0 >> gs_log2, sc[k][v], zr[k][v]);
+      }
+    }
+#pragma unroll
+  for (int k = 0; k < TPW; ++k)
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      const int t = base + lane + 32 * v;
+      if (t >= ntasks[k]) continue;
+      float f[EPT];
+#pragma unroll
+      for (int e = 0; e < EPT; ++e) {
+        float qv;
+        if (BITS == 8) {
+          qv = code_byte(e < 4 ? cw[k][v].x : cw[k][v].y, e & 3);
+        } else {  // element e is nibble e: the low nibble of byte e/2 for even e
+          const uint32_t w = cw[k][v].x;
+          qv = code_byte((e & 1) ? ((w >> 4) & 0x0F0F0F0Fu) : (w & 0x0F0F0F0Fu), e >> 1);
+        }
+        f[e] = __fadd_rn(__fmul_rn(qv, sc[k][v]), zr[k][v]);
+      }
+      Store16<OUT_DT>::run(out[k] + (int64_t)t * 16, f);
+    }
+}
+
+// Persistent CTAs, two CTAs of 256 threads per SM; each warp dequantises
+// two tiles per round.  POW2: head_dim / EPT is a power of two (2^tpr_log2)
+// and a task's row is found by a shift, else by division.  A tile with at
+// most 32 * V tasks (every 16 x 128 bf16/f16 tile) takes one round with a
+// compile-time base of 0.
+template <int BITS, int OUT_DT, bool META_F32, bool POW2>
+__global__ void __launch_bounds__(256, 2) gather_dequant_kernel(PoolGeo g, int layer, const int32_t* __restrict__ bt,
+                                                                int bt_stride, const int32_t* __restrict__ lens,
+                                                                int nseq, uint8_t* __restrict__ ok,
+                                                                uint8_t* __restrict__ ov, int hd, int gs_log2,
+                                                                int tpr_log2, int32_t* err) {
+  constexpr int EPT = Store16<OUT_DT>::n;
+  constexpr int V = 8;    // tasks per lane per tile per round
+  constexpr int TPW = 2;  // tiles per warp per round
   extern __shared__ int32_t smem[];
   int32_t* cub = smem;
   int32_t* cut = smem + nseq + 1;
   scan_seq_lens(lens, nseq, g.bs, cub, cut);
   const int64_t units = (int64_t)cub[nseq] * 2 * g.heads;
   const int lane = threadIdx.x & 31;
-  const int cpr = g.row_bytes / 16;
+  const int tpr = hd / EPT;  // tasks per row
+  const int64_t orb = (int64_t)hd * (16 / EPT);
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  for (int64_t u = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; u < units; u += nwarps) {
-    int h = (int)(u % g.heads);
-    int64_t q = u / g.heads;
-    int kv = (int)(q & 1);
-    int64_t gi = q >> 1;
-    int s = find_seq(cub, nseq, gi);
-    int b = (int)(gi - cub[s]);
-    int L = cut[s + 1] - cut[s];
-    int nrows = min(g.bs, L - b * g.bs);
-    int32_t blk = __ldg(bt + (int64_t)s * bt_stride + b);
-    if (blk < 0 || blk >= g.nblocks) {
-      if (lane == 0) atomicOr(err, DEV_ERR_BLOCK);
-      continue;
+  for (int64_t u0 = ((blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5) * TPW; u0 < units;
+       u0 += nwarps * TPW) {
+    const uint8_t* tile[TPW];
+    uint8_t* out[TPW];
+    int ntasks[TPW];
+    int nmax = 0;
+#pragma unroll
+    for (int k = 0; k < TPW; ++k) {
+      const int64_t u = u0 + k;
+      tile[k] = nullptr;
+      out[k] = nullptr;
+      ntasks[k] = 0;
+      if (u >= units) continue;
+      const int h = (int)(u % g.heads);
+      const int64_t q = u / g.heads;
+      const int kv = (int)(q & 1);
+      const int64_t gi = q >> 1;
+      const int s = find_seq(cub, nseq, gi);
+      const int b = (int)(gi - cub[s]);
+      const int L = cut[s + 1] - cut[s];
+      const int32_t blk = __ldg(bt + (int64_t)s * bt_stride + b);
+      if (blk < 0 || blk >= g.nblocks) {
+        if (lane == 0) atomicOr(err, DEV_ERR_BLOCK);
+        continue;
+      }
+      tile[k] = g.base + g.tile_off(blk, layer, kv, h);
+      out[k] = (kv ? ov : ok) + ((int64_t)cut[s] * g.heads + (int64_t)h * L + (int64_t)b * g.bs) * orb;
+      ntasks[k] = min(g.bs, L - b * g.bs) * tpr;
+      nmax = max(nmax, ntasks[k]);
     }
-    const uint8_t* tile = g.base + g.tile_off(blk, layer, kv, h);
-    const uint8_t* meta = tile + (int64_t)g.bs * g.row_bytes;
-    uint8_t* out = (kv ? ov : ok) + ((int64_t)cut[s] * g.heads + (int64_t)h * L + (int64_t)b * g.bs) * hd * E::size;
-    const int n16 = nrows * cpr;
-    for (int base = 0; base < n16; base += 32 * U) {
-      uint4 cw[U];
-#pragma unroll
-      for (int j = 0; j < U; ++j) {
-        int idx = base + lane + 32 * j;
-        if (idx < n16) cw[j] = ld_stream(tile + (int64_t)idx * 16);
-      }
-#pragma unroll
-      for (int j = 0; j < U; ++j) {
-        int idx = base + lane + 32 * j;
-        if (idx >= n16) continue;
-        const int r = idx / cpr, e0 = (idx - r * cpr) * EPC;
-        const uint8_t* mrow = meta + (int64_t)r * g.meta_row_bytes;
-        const uint32_t w[4] = {cw[j].x, cw[j].y, cw[j].z, cw[j].w};
-        uint8_t* orow = out + ((int64_t)r * hd + e0) * E::size;
-        float sc = 0.0f, zr = 0.0f;
-        if (ONE_GROUP) {
-          const int gq = e0 >> gs_log2;
-          if (META_F32) {
-            sc = __ldg(reinterpret_cast<const float*>(mrow) + 2 * gq);
-            zr = __ldg(reinterpret_cast<const float*>(mrow) + 2 * gq + 1);
-          } else {
-            float2 m = __half22float2(__ldg(reinterpret_cast<const __half2*>(mrow) + gq));
-            sc = m.x;
-            zr = m.y;
-          }
-        }
-#pragma unroll
-        for (int o8 = 0; o8 < EPC / 8; ++o8) {
-          float f[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const int el = o8 * 8 + e;  // element within the chunk
-            uint32_t code;
-            if (BITS == 8) code = (w[el >> 2] >> (8 * (el & 3))) & 0xffu;
-            else code = (w[el >> 3] >> (4 * (el & 7))) & 0xfu;
-            if (!ONE_GROUP) {
-              const int gq = (e0 + el) >> gs_log2;
-              if (META_F32) {
-                sc = __ldg(reinterpret_cast<const float*>(mrow) + 2 * gq);
-                zr = __ldg(reinterpret_cast<const float*>(mrow) + 2 * gq + 1);
-              } else {
-                float2 m = __half22float2(__ldg(reinterpret_cast<const __half2*>(mrow) + gq));
-                sc = m.x;
-                zr = m.y;
-              }
-            }
-            f[e] = __fadd_rn(__fmul_rn((float)code, sc), zr);
-          }
-          E::store8(orow + o8 * 8 * E::size, f);
-        }
-      }
+    if (nmax <= 32 * V) {
+      dq_round<BITS, OUT_DT, META_F32, POW2, TPW, V>(g, tile, out, ntasks, 0, lane, tpr, tpr_log2, gs_log2);
+    } else {
+      for (int base = 0; base < nmax; base += 32 * V)
+        dq_round<BITS, OUT_DT, META_F32, POW2, TPW, V>(g, tile, out, ntasks, base, lane, tpr, tpr_log2, gs_log2);
     }
   }
 }
@@ -514,6 +602,10 @@ struct rmlx_kv_pool {
   int32_t* err = nullptr;
   size_t bytes = 0, tile_bytes = 0, block_bytes = 0, row_bytes = 0, meta_row_bytes = 0;
   int num_sms = 148;
+  // Persistent-grid size of this pool's gather kernel for the last dynamic
+  // shared-memory size used (the kernel is fixed by the pool's config).
+  size_t gather_smem = 0;
+  int gather_grid = 0;
   PoolGeo geo() const {
     PoolGeo g;
     g.base = base;
@@ -570,19 +662,19 @@ AppendQuantFn pick_append_quant(int in_dt, int bits, bool mf32) {
 }
 
 using GatherDqFn = void (*)(PoolGeo, int, const int32_t*, int, const int32_t*, int, uint8_t*, uint8_t*, int, int,
-                            int32_t*);
-template <int BITS, int OUT, bool MF32, bool ONE>
+                            int, int32_t*);
+template <int BITS, int OUT, bool MF32, bool POW2>
 GatherDqFn gd() {
-  return gather_dequant_kernel<BITS, OUT, MF32, ONE>;
+  return gather_dequant_kernel<BITS, OUT, MF32, POW2>;
 }
-GatherDqFn pick_gather_dequant(int bits, int out_dt, bool mf32, bool one) {
+GatherDqFn pick_gather_dequant(int bits, int out_dt, bool mf32, bool pow2) {
 #define GD_ROW(B, O) {{gd<B, O, false, false>(), gd<B, O, false, true>()}, {gd<B, O, true, false>(), gd<B, O, true, true>()}}
   static const GatherDqFn t[2][3][2][2] = {
       {GD_ROW(4, 0), GD_ROW(4, 1), GD_ROW(4, 2)},
       {GD_ROW(8, 0), GD_ROW(8, 1), GD_ROW(8, 2)},
   };
 #undef GD_ROW
-  return t[bits == 8][out_dt][mf32][one];
+  return t[bits == 8][out_dt][mf32][pow2];
 }
 
 }  // namespace
@@ -740,18 +832,26 @@ rmlx_status rmlx_kv_gather(rmlx_kv_pool* p, int32_t layer, const int32_t* bt, in
   PoolGeo g = p->geo();
   const size_t smem = (size_t)(nseq + 1) * 2 * sizeof(int32_t);
   rmlx_status s;
+  const bool fresh = p->gather_grid == 0 || p->gather_smem != smem;
   if (c.quant_bits == 0) {
-    if ((s = prepare_smem(gather_rows_kernel, smem)) != RMLX_OK) return s;
-    const int grid = persistent_grid(gather_rows_kernel, 256, smem, p->num_sms);
-    gather_rows_kernel<<<grid, 256, smem, st>>>(g, layer, bt, bt_stride, lens, nseq, (uint8_t*)out_k, (uint8_t*)out_v,
-                                                p->err);
+    if (fresh) {
+      if ((s = prepare_smem(gather_rows_kernel, smem)) != RMLX_OK) return s;
+      p->gather_grid = persistent_grid(gather_rows_kernel, 256, smem, p->num_sms);
+      p->gather_smem = smem;
+    }
+    gather_rows_kernel<<<p->gather_grid, 256, smem, st>>>(g, layer, bt, bt_stride, lens, nseq, (uint8_t*)out_k,
+                                                          (uint8_t*)out_v, p->err);
   } else {
-    const int epc = c.quant_bits == 8 ? 16 : 32;
-    GatherDqFn fn = pick_gather_dequant(c.quant_bits, c.dtype, c.meta_dtype == RMLX_F32, c.group_size % epc == 0);
-    if ((s = prepare_smem(fn, smem)) != RMLX_OK) return s;
-    const int grid = persistent_grid(fn, 256, smem, p->num_sms);
-    fn<<<grid, 256, smem, st>>>(g, layer, bt, bt_stride, lens, nseq, (uint8_t*)out_k, (uint8_t*)out_v, c.head_dim,
-                                log2i(c.group_size), p->err);
+    const int ept = c.dtype == RMLX_F32 ? 4 : 8;  // output elements per 16-byte task
+    const int tpr = c.head_dim / ept;
+    GatherDqFn fn = pick_gather_dequant(c.quant_bits, c.dtype, c.meta_dtype == RMLX_F32, is_pow2(tpr));
+    if (fresh) {
+      if ((s = prepare_smem(fn, smem)) != RMLX_OK) return s;
+      p->gather_grid = persistent_grid(fn, 256, smem, p->num_sms);
+      p->gather_smem = smem;
+    }
+    fn<<<p->gather_grid, 256, smem, st>>>(g, layer, bt, bt_stride, lens, nseq, (uint8_t*)out_k, (uint8_t*)out_v,
+                                          c.head_dim, log2i(c.group_size), is_pow2(tpr) ? log2i(tpr) : -1, p->err);
   }
   return cuda_check(cudaGetLastError(), "gather launch");
 }
