@@ -395,16 +395,20 @@ def main():
     out_v = torch.empty_like(out_k)
     ls = B * H * D
 
-    def launch_step(s, ev_pairs=None):
+    def launch_step(s, ev_pair=None):
+        """The append, then the gather of every layer.  ev_pair brackets the
+        step's gathers (not each launch: events between launches would stop
+        consecutive kernels from overlapping their launch with the tail of
+        the previous one)."""
         rc = lib.rmlx_kv_append(h, 0, L, new_k[s].data_ptr(), new_v[s].data_ptr(), ls, ts, hs,
                                 slots_d[s].data_ptr(), B, sp)
+        if ev_pair is not None:
+            ev_pair[0].record(stream)
         for layer in range(L):
-            if ev_pairs is not None:
-                ev_pairs[layer][0].record(stream)
             rc |= lib.rmlx_kv_gather(h, layer, bt_d.data_ptr(), bt.shape[1], lens_d[s].data_ptr(), B,
                                      out_k.data_ptr(), out_v.data_ptr(), sp)
-            if ev_pairs is not None:
-                ev_pairs[layer][1].record(stream)
+        if ev_pair is not None:
+            ev_pair[1].record(stream)
         return rc
 
     def barrier():
@@ -426,8 +430,7 @@ def main():
 
     clocks = Clocks(dev)
     clocks.start()
-    ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(L)]
-          for _ in range(K)]
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
@@ -438,7 +441,8 @@ def main():
     torch.cuda.synchronize()
     barrier()
     elapsed_ms = max_over_ranks(e0.elapsed_time(e1))
-    gather_ms = [ev[i][l][0].elapsed_time(ev[i][l][1]) for i in range(K) for l in range(L)]
+    # average gather launch = a step's gather span / its L launches
+    gather_ms = [ev[i][0].elapsed_time(ev[i][1]) / L for i in range(K)]
     if rc or pool.check() != 0:
         raise SystemExit("launch or device-side validation error in the timed region")
 

@@ -331,6 +331,35 @@ RMLX_API rmlx_status rmlx_hash_block_chains(const uint32_t* tokens, const int64_
                                    int32_t num_requests, int32_t block_size, const int64_t* cu_blocks,
                                    uint64_t* out, void* stream);
 
+/* ======================================================================
+ * Cross-GPU block migration (NCCL over NVLink / NVSwitch).  The reference's
+ * only multi-device hook is the never-enabled "distributed" feature of
+ * rmlx-serve-engine (crates/rmlx-serve-engine/Cargo.toml:24-30); with the pool
+ * sharded by KV head, moving blocks between pools on different GPUs is the
+ * one exchange: pack -> grouped ncclSend/ncclRecv -> unpack on one stream.
+ * Communicators are non-blocking; every wait is bounded by timeout_ms, after
+ * which the communicator is aborted and RMLX_E_TIMEOUT is returned.
+ * ==================================================================== */
+typedef struct rmlx_comm rmlx_comm;
+#define RMLX_NCCL_ID_BYTES 128
+
+/* 128-byte NCCL unique id, made on one rank and shared with the others. */
+RMLX_API rmlx_status rmlx_nccl_unique_id(uint8_t* out);
+/* Communicator of `nranks` processes; this one is `rank`, on `device`. */
+RMLX_API rmlx_status rmlx_nccl_comm_new(int32_t nranks, const uint8_t* id, int32_t rank, int device,
+                                        int32_t timeout_ms, rmlx_comm** out);
+RMLX_API void rmlx_nccl_comm_destroy(rmlx_comm* c);
+/* Exchange blocks with `peer` (both ranks call it): send blocks send_ids
+ * (device array, n_send) of this pool, receive n_recv blocks into recv_ids.
+ * Staging buffers are device buffers of n * block_bytes.  Enqueued on
+ * `stream`; rmlx_nccl_wait bounds the completion. */
+RMLX_API rmlx_status rmlx_kv_migrate(rmlx_kv_pool* p, rmlx_comm* c, int32_t peer, const int32_t* send_ids,
+                                     int32_t n_send, void* send_staging, const int32_t* recv_ids, int32_t n_recv,
+                                     void* recv_staging, void* stream);
+/* Wait for `stream` (timeout_ms <= 0: the communicator's timeout); on an
+ * NCCL error or the deadline the communicator is aborted. */
+RMLX_API rmlx_status rmlx_nccl_wait(rmlx_comm* c, void* stream, int32_t timeout_ms);
+
 #ifdef __cplusplus
 }
 #endif

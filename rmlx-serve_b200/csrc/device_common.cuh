@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <utility>
 
 #include "common.h"
 
@@ -75,6 +76,32 @@ __device__ __forceinline__ void warp_copy2(const uint8_t* sa, uint8_t* da, int n
       if (c < n16b) st_stream(db + (size_t)c * 16, rb[j]);
     }
   }
+}
+
+// Programmatic dependent launch.  Kernels are launched with programmatic
+// stream serialisation, so the next kernel in the stream may be scheduled
+// before this one finishes; pdl_wait() (at the top of every kernel, before
+// any global memory access) blocks until the preceding grid has completed
+// and its writes are visible, and pdl_release() lets the next grid start
+// launching.  Without the launch attribute both are no-ops.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_release() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Launch with programmatic stream serialisation (see pdl_wait).
+template <typename... Exp, typename... Act>
+cudaError_t launch_pdl(void (*kernel)(Exp...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Act&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Act>(args)...);
 }
 
 // RAII switch of the current device for the duration of an API call.

@@ -44,6 +44,8 @@ __global__ void __launch_bounds__(256) append_rows_kernel(PoolGeo g, int l0, int
                                                           const uint8_t* __restrict__ v, int64_t ls, int64_t ts,
                                                           int64_t hs, const int32_t* __restrict__ slots, int T,
                                                           int cpr, int32_t* err) {
+  pdl_wait();
+  pdl_release();
   const int64_t total = (int64_t)nl * T * 2 * g.heads * cpr;
   const int64_t cap = (int64_t)g.nblocks * g.bs;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
@@ -182,6 +184,8 @@ __global__ void __launch_bounds__(256, 2) gather_rows_kernel(PoolGeo g, int laye
   extern __shared__ int32_t smem[];
   int32_t* cub = smem;
   int32_t* cut = smem + nseq + 1;
+  pdl_wait();
+  pdl_release();
   scan_seq_lens(lens, nseq, g.bs, cub, cut);
   const int64_t units = (int64_t)cub[nseq] * 2 * g.heads;
   const int lane = threadIdx.x & 31;
@@ -276,6 +280,8 @@ __global__ void __launch_bounds__(256) append_quant_kernel(PoolGeo g, int l0, in
                                                            int64_t hs, const int32_t* __restrict__ slots, int T,
                                                            int hd, int tpg, int32_t* err) {
   using E = Elem<IN_DT>;
+  pdl_wait();
+  pdl_release();
   const int cpr = hd / 8;
   const int64_t total = (int64_t)nl * T * 2 * g.heads * cpr;
   const int64_t cap = (int64_t)g.nblocks * g.bs;
@@ -494,6 +500,8 @@ __global__ void __launch_bounds__(256, 2) gather_dequant_kernel(PoolGeo g, int l
   extern __shared__ int32_t smem[];
   int32_t* cub = smem;
   int32_t* cut = smem + nseq + 1;
+  pdl_wait();
+  pdl_release();
   scan_seq_lens(lens, nseq, g.bs, cub, cut);
   const int64_t units = (int64_t)cub[nseq] * 2 * g.heads;
   const int lane = threadIdx.x & 31;
@@ -577,6 +585,8 @@ __global__ void __launch_bounds__(256, 2) copy_blocks_kernel(uint8_t* base, int6
                                                              const int32_t* __restrict__ src,
                                                              const int32_t* __restrict__ dst, int n, int mode,
                                                              uint8_t* staging, int32_t* err) {
+  pdl_wait();
+  pdl_release();
   const int64_t segs = (block_bytes + 4095) / 4096;
   const int64_t units = (int64_t)n * segs;
   const int lane = threadIdx.x & 31;
@@ -805,13 +815,17 @@ rmlx_status rmlx_kv_append(rmlx_kv_pool* p, int32_t layer_begin, int32_t num_lay
     const int cpr = (int)(p->row_bytes / 16);
     const int64_t total = (int64_t)num_layers * T * 2 * c.num_kv_heads * cpr;
     const int grid = (int)std::min<int64_t>((total + 255) / 256, (int64_t)p->num_sms * 16);
-    append_rows_kernel<<<grid, 256, 0, st>>>(g, layer_begin, num_layers, kb, vb, ls, ts, hs, slots, T, cpr, p->err);
+    cudaError_t e = launch_pdl(append_rows_kernel, dim3(grid), dim3(256), 0, st, g, layer_begin, num_layers, kb, vb, ls,
+                               ts, hs, slots, T, cpr, p->err);
+    if (e != cudaSuccess) return cuda_check(e, "append launch");
   } else {
     const int tpg = c.group_size / 8;
     const int64_t total = (int64_t)num_layers * T * 2 * c.num_kv_heads * (c.head_dim / 8);
     const int grid = (int)std::min<int64_t>((total + 255) / 256, (int64_t)p->num_sms * 16);
     AppendQuantFn fn = pick_append_quant(c.dtype, c.quant_bits, c.meta_dtype == RMLX_F32);
-    fn<<<grid, 256, 0, st>>>(g, layer_begin, num_layers, kb, vb, ls, ts, hs, slots, T, c.head_dim, tpg, p->err);
+    cudaError_t e = launch_pdl(fn, dim3(grid), dim3(256), 0, st, g, layer_begin, num_layers, kb, vb, ls, ts, hs, slots,
+                               T, c.head_dim, tpg, p->err);
+    if (e != cudaSuccess) return cuda_check(e, "append launch");
   }
   return cuda_check(cudaGetLastError(), "append launch");
 }
@@ -839,8 +853,9 @@ rmlx_status rmlx_kv_gather(rmlx_kv_pool* p, int32_t layer, const int32_t* bt, in
       p->gather_grid = persistent_grid(gather_rows_kernel, 256, smem, p->num_sms);
       p->gather_smem = smem;
     }
-    gather_rows_kernel<<<p->gather_grid, 256, smem, st>>>(g, layer, bt, bt_stride, lens, nseq, (uint8_t*)out_k,
-                                                          (uint8_t*)out_v, p->err);
+    cudaError_t e = launch_pdl(gather_rows_kernel, dim3(p->gather_grid), dim3(256), smem, st, g, layer, bt, bt_stride,
+                               lens, nseq, (uint8_t*)out_k, (uint8_t*)out_v, p->err);
+    if (e != cudaSuccess) return cuda_check(e, "gather launch");
   } else {
     const int ept = c.dtype == RMLX_F32 ? 4 : 8;  // output elements per 16-byte task
     const int tpr = c.head_dim / ept;
@@ -850,8 +865,10 @@ rmlx_status rmlx_kv_gather(rmlx_kv_pool* p, int32_t layer, const int32_t* bt, in
       p->gather_grid = persistent_grid(fn, 256, smem, p->num_sms);
       p->gather_smem = smem;
     }
-    fn<<<p->gather_grid, 256, smem, st>>>(g, layer, bt, bt_stride, lens, nseq, (uint8_t*)out_k, (uint8_t*)out_v,
-                                          c.head_dim, log2i(c.group_size), is_pow2(tpr) ? log2i(tpr) : -1, p->err);
+    cudaError_t e = launch_pdl(fn, dim3(p->gather_grid), dim3(256), smem, st, g, layer, bt, bt_stride, lens, nseq,
+                               (uint8_t*)out_k, (uint8_t*)out_v, (int)c.head_dim, log2i(c.group_size),
+                               is_pow2(tpr) ? log2i(tpr) : -1, p->err);
+    if (e != cudaSuccess) return cuda_check(e, "gather launch");
   }
   return cuda_check(cudaGetLastError(), "gather launch");
 }
@@ -866,8 +883,9 @@ static rmlx_status launch_copy(rmlx_kv_pool* p, const int32_t* a, const int32_t*
   DeviceGuard dg(p->device);
   const int64_t units = (int64_t)n * (((int64_t)p->block_bytes + 4095) / 4096);
   const int grid = (int)std::min<int64_t>((units + 15) / 16, (int64_t)p->num_sms * 2);
-  copy_blocks_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(p->base, (int64_t)p->block_bytes, p->cfg.num_blocks, a,
-                                                             b, n, mode, staging, p->err);
+  cudaError_t e = launch_pdl(copy_blocks_kernel, dim3(grid), dim3(256), 0, (cudaStream_t)stream, p->base,
+                             (int64_t)p->block_bytes, (int)p->cfg.num_blocks, a, b, n, mode, staging, p->err);
+  if (e != cudaSuccess) return cuda_check(e, "copy_blocks launch");
   return cuda_check(cudaGetLastError(), "copy_blocks launch");
 }
 

@@ -144,3 +144,10 @@ _sig("rmlx_kv_copy_blocks", st, vp, vp, vp, C.c_int32, vp)
 _sig("rmlx_kv_pack_blocks", st, vp, vp, C.c_int32, vp, vp)
 _sig("rmlx_kv_unpack_blocks", st, vp, vp, C.c_int32, vp, vp)
 _sig("rmlx_hash_block_chains", st, vp, vp, vp, C.c_int32, C.c_int32, vp, vp, vp)
+
+# NCCL migration
+_sig("rmlx_nccl_unique_id", st, u8p)
+_sig("rmlx_nccl_comm_new", st, C.c_int32, u8p, C.c_int32, C.c_int, C.c_int32, C.POINTER(vp))
+_sig("rmlx_nccl_comm_destroy", None, vp)
+_sig("rmlx_kv_migrate", st, vp, vp, C.c_int32, vp, C.c_int32, vp, vp, C.c_int32, vp, vp)
+_sig("rmlx_nccl_wait", st, vp, vp, C.c_int32)

@@ -122,6 +122,49 @@ class KVPool:
     def unpack_blocks(self, ids, n: int, staging, stream=None) -> None:
         check(lib.rmlx_kv_unpack_blocks(self._h, _ptr(ids), n, _ptr(staging), _stream(stream, self.device)))
 
+    def migrate(self, comm, peer: int, send_ids, n_send: int, send_staging, recv_ids, n_recv: int, recv_staging,
+                stream=None) -> None:
+        """Send blocks to `peer` and receive blocks from it (both ranks call this)."""
+        check(lib.rmlx_kv_migrate(self._h, comm.handle, peer, _ptr(send_ids), n_send, _ptr(send_staging),
+                                  _ptr(recv_ids), n_recv, _ptr(recv_staging), _stream(stream, self.device)))
+
+
+class NcclComm:
+    """NCCL communicator for block migration (one process per GPU).
+
+    Rank 0 makes the id with ``NcclComm.unique_id()`` and shares it with the
+    other ranks (any host channel); every rank then constructs the comm.
+    """
+
+    def __init__(self, nranks: int, uid: bytes, rank: int, device: int, timeout_ms: int = 60000):
+        if len(uid) != 128:
+            raise ValueError("NCCL unique id must be 128 bytes")
+        buf = (C.c_uint8 * 128).from_buffer_copy(uid)
+        h = _lib.vp()
+        check(lib.rmlx_nccl_comm_new(nranks, buf, rank, device, timeout_ms, C.byref(h)))
+        self._h, self.rank, self.nranks, self.device = h, rank, nranks, device
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = (C.c_uint8 * 128)()
+        check(lib.rmlx_nccl_unique_id(buf))
+        return bytes(buf)
+
+    @property
+    def handle(self):
+        return self._h
+
+    def wait(self, stream=None, timeout_ms: int = 0) -> None:
+        check(lib.rmlx_nccl_wait(self._h, _stream(stream, self.device), timeout_ms))
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib.rmlx_nccl_comm_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
 
 def hash_block_chains(tokens, cu_tokens, root_hashes, num_requests: int, block_size: int, cu_blocks, out,
                       stream=None, device: int = 0) -> None:

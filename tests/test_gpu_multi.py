@@ -1,0 +1,88 @@
+"""Two-GPU block migration over NCCL (pack -> ncclSend/ncclRecv -> unpack).
+
+Runs as two spawned child processes, one per GPU, and is skipped when fewer
+than two GPUs are visible.  Each rank fills its pool with bytes derived
+from its rank, the ranks exchange blocks in both directions, and every
+migrated block must arrive bit-identical; blocks that were not targets
+must be untouched.
+"""
+import multiprocessing as mp
+import os
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+L, H, D, BS, N = 2, 2, 128, 16, 64
+SEND = {0: [3, 7, 9, 63], 1: [1, 2]}     # blocks each rank sends
+RECV = {0: [20, 21], 1: [10, 11, 12, 0]}  # where each rank puts what it receives
+
+
+def _pool_bytes(rank, nbytes):
+    return np.random.default_rng(1000 + rank).integers(0, 256, size=nbytes, dtype=np.uint8)
+
+
+def _worker(rank, uid_q, res_q):
+    try:
+        import sys
+        root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+        sys.path.insert(0, os.path.join(root, "rmlx-serve_b200"))
+        import torch
+        import rmlx_kv
+        torch.cuda.set_device(rank)
+        if rank == 0:
+            uid = rmlx_kv.NcclComm.unique_id()
+            uid_q.put(uid)
+        else:
+            uid = uid_q.get(timeout=60)
+        pool = rmlx_kv.KVPool(L, H, D, BS, N, dtype=rmlx_kv.BF16, device=rank)
+        bb = pool.layout.block_bytes
+        mine = _pool_bytes(rank, pool.layout.bytes)
+        pool.write(mine)
+        comm = rmlx_kv.NcclComm(2, uid, rank, rank, timeout_ms=60000)
+        peer = 1 - rank
+        send = torch.tensor(SEND[rank], dtype=torch.int32, device="cuda")
+        recv = torch.tensor(RECV[rank], dtype=torch.int32, device="cuda")
+        s_st = torch.empty(len(SEND[rank]) * bb, dtype=torch.uint8, device="cuda")
+        r_st = torch.empty(len(RECV[rank]) * bb, dtype=torch.uint8, device="cuda")
+        pool.migrate(comm, peer, send, len(SEND[rank]), s_st, recv, len(RECV[rank]), r_st)
+        comm.wait(timeout_ms=60000)
+        got = pool.read()
+        theirs = _pool_bytes(peer, pool.layout.bytes)
+        want = mine.copy()
+        for src, dst in zip(SEND[peer], RECV[rank]):
+            want[dst * bb:(dst + 1) * bb] = theirs[src * bb:(src + 1) * bb]
+        ok = bool(np.array_equal(got, want)) and pool.check() == 0
+        comm.close()
+        pool.close()
+        res_q.put((rank, ok, ""))
+    except Exception as e:  # reported to the parent, which fails the test
+        res_q.put((rank, False, repr(e)))
+
+
+def test_migrate_blocks_between_two_gpus():
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    uid_q, res_q = ctx.Queue(), ctx.Queue()
+    env_keep = os.environ.get("NCCL_NVLS_ENABLE")
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    try:
+        procs = [ctx.Process(target=_worker, args=(r, uid_q, res_q)) for r in range(2)]
+        for p in procs:
+            p.start()
+        results = [res_q.get(timeout=240) for _ in range(2)]
+        for p in procs:
+            p.join(timeout=60)
+    finally:
+        if env_keep is None:
+            os.environ.pop("NCCL_NVLS_ENABLE", None)
+        else:
+            os.environ["NCCL_NVLS_ENABLE"] = env_keep
+        for p in procs:
+            if p.is_alive():
+                p.kill()
+    for rank, ok, err in sorted(results):
+        assert ok, f"rank {rank}: {err or 'migrated blocks differ'}"
