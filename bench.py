@@ -8,6 +8,13 @@ layer, then gathers every layer's K/V for all sequences through the block
 tables.  Block tables are drawn from a seeded permutation of a pool sized
 1.25x the blocks in use.
 
+``--workload prefix``: prefix caching with eviction -- 512 requests, token
+ids uniform over 128256; 60% start with one of 8 shared 1024-token prefixes
+plus a unique 64-512-token suffix, 40% are unique with 256-2048 tokens;
+per-block chain hashes on the GPU, then admission through the block manager
+and the prefix cache with LRU eviction under a pool of 60% of the distinct
+blocks the requests need.  Metric: admissions per second.
+
 ``--workload quant8`` / ``quant4``: the same layers and heads, batch 128,
 contexts uniform in [1024, 8192], K/V N(0,1) with 1% outliers x8, stored as
 8-bit / 4-bit group-affine codes (group 64 along head_dim, fp16 scale and
@@ -96,6 +103,126 @@ WORKLOADS = {
         "dequantise-on-gather (bf16) of every layer", seed=0x5EED + 3, batch=128, ctx_lo=1024, ctx_hi=8192, bits=4,
         outliers=0.01),
 }
+
+
+PREFIX_METRIC = "prefix-cache admissions/s (512 requests, 8 shared 1024-token prefixes, LRU at 60% budget)"
+PREFIX_DESC = ("prefix caching + eviction: 512 requests, vocab 128256; 60% = one of 8 shared 1024-token prefixes + "
+               "unique 64-512-token suffix, 40% unique 256-2048 tokens; chain hash per 16-token block + parent on the "
+               "GPU; refcounted reuse; LRU eviction with a pool of 60% of the distinct blocks needed")
+
+
+def prefix_requests(seed, n_req=512, n_prefix=8, prefix_len=1024, suffix=(64, 512), unique=(256, 2048),
+                    vocab=128256, shared=0.6):
+    """Seeded requests of the prefix-caching workload: (tokens, cu_tokens)."""
+    rng = np.random.default_rng(seed)
+    prefixes = [rng.integers(0, vocab, size=prefix_len, dtype=np.uint32) for _ in range(n_prefix)]
+    reqs = []
+    for _ in range(n_req):
+        if rng.random() < shared:
+            p = prefixes[int(rng.integers(n_prefix))]
+            reqs.append(np.concatenate([p, rng.integers(0, vocab, size=int(rng.integers(suffix[0], suffix[1] + 1)),
+                                                        dtype=np.uint32)]))
+        else:
+            reqs.append(rng.integers(0, vocab, size=int(rng.integers(unique[0], unique[1] + 1)), dtype=np.uint32))
+    cu = np.zeros(n_req + 1, dtype=np.int64)
+    cu[1:] = np.cumsum([len(r) for r in reqs])
+    return np.concatenate(reqs).astype(np.uint32), cu
+
+
+def prefix_pool_size(toks, cu, cub, hashes, block=16):
+    """60% of the distinct blocks the requests need (a dry run with room for all)."""
+    import rmlx_kv
+    m, p = rmlx_kv.PagedCacheManager(block, int(cub[-1])), rmlx_kv.PrefixCacheManager(int(cub[-1]))
+    _, _, st = rmlx_kv.prefix_admit(m, p, toks, cu, hashes, cub)
+    return int(np.ceil(0.6 * st["new_blocks"]))
+
+
+def run_prefix(args, rank, world):
+    """GPU chain hash of every block + native admission; rank 0 only (the
+    prefix cache is replicated on every rank, so the work does not shard)."""
+    if rank != 0:
+        return
+    import torch
+    import rmlx_kv
+    torch.cuda.set_device(0)
+    seed = 0x5EED + 4
+    toks, cu = prefix_requests(seed)
+    nb = (np.diff(cu) + 15) // 16
+    cub = np.zeros(len(cu), dtype=np.int64)
+    cub[1:] = np.cumsum(nb)
+    n_req = len(cu) - 1
+    stream = torch.cuda.current_stream()
+    d_t, d_cu, d_cub = (torch.from_numpy(toks.view(np.int32)).cuda(), torch.from_numpy(cu).cuda(),
+                        torch.from_numpy(cub).cuda())
+    d_h = torch.empty(int(cub[-1]), dtype=torch.int64, device="cuda")
+    for _ in range(args.warmup):
+        rmlx_kv.hash_block_chains(d_t, d_cu, None, n_req, 16, d_cub, d_h)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        rmlx_kv.hash_block_chains(d_t, d_cu, None, n_req, 16, d_cub, d_h)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    hash_ms = e0.elapsed_time(e1) / args.steps
+    hashes = d_h.cpu().numpy().view(np.uint64)
+    pool = prefix_pool_size(toks, cu, cub, hashes)
+    admit_s, stats = [], None
+    for i in range(args.warmup + args.steps):
+        m, p = rmlx_kv.PagedCacheManager(16, pool), rmlx_kv.PrefixCacheManager(pool)
+        t0 = time.perf_counter()
+        _, ev, stats = rmlx_kv.prefix_admit(m, p, toks, cu, hashes, cub)
+        if i >= args.warmup:
+            admit_s.append(time.perf_counter() - t0)
+        hit = p.hit_rate()
+    admit = float(np.median(admit_s))
+    # e2e: tokens H2D, hash kernel, hashes D2H, admission -- per batch of requests
+    pin_t = torch.from_numpy(toks.view(np.int32)).pin_memory()
+    pin_h = torch.empty(int(cub[-1]), dtype=torch.int64, pin_memory=True)
+    e2e = []
+    for i in range(args.warmup + args.steps):
+        m, p = rmlx_kv.PagedCacheManager(16, pool), rmlx_kv.PrefixCacheManager(pool)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        d_t.copy_(pin_t, non_blocking=True)
+        rmlx_kv.hash_block_chains(d_t, d_cu, None, n_req, 16, d_cub, d_h)
+        pin_h.copy_(d_h, non_blocking=True)
+        torch.cuda.synchronize()
+        rmlx_kv.prefix_admit(m, p, toks, cu, pin_h.numpy().view(np.uint64), cub)
+        if i >= args.warmup:
+            e2e.append(time.perf_counter() - t0)
+    e2e_s = float(np.median(e2e))
+    cpu = None
+    if not args.no_cpu_baseline:
+        gbs, sec = prefix_cpu(toks, cu, cub, pool)
+        cpu = {"value": round(n_req / sec, 2), "unit": "admissions/s", "cores": 1, "kind": "port",
+               "sample": "oracle chain hash + admission of all 512 requests (single thread, as the reference)"}
+    hash_bytes = 4 * len(toks) + 8 * int(cub[-1])
+    print(json.dumps({
+        "metric": PREFIX_METRIC, "value": round(n_req / (hash_ms * 1e-3 + admit), 2), "unit": "admissions/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(hash_ms + admit * 1e3, 4), "us_per_admission": round(admit / n_req * 1e6, 2),
+        "higher_is_better": True, "scaling": "replicas", "vs_baseline": None, "dtype": "u32", "data": "synthetic",
+        "config": {"workload": PREFIX_DESC, "requests": n_req, "tokens": int(len(toks)), "blocks": int(cub[-1]),
+                   "pool_blocks": pool},
+        "hash_kernel": {"ms": round(hash_ms, 4), "gbs": round(hash_bytes / (hash_ms * 1e-3) / 1e9, 2)},
+        "admission": {"ms": round(admit * 1e3, 3), **stats, "hit_rate": round(hit, 4)},
+        "e2e": {"value": round(n_req / e2e_s, 2), "unit": "admissions/s", "h2d_bytes_per_step": 4 * len(toks),
+                "d2h_bytes_per_step": 8 * int(cub[-1])},
+        "gpu_launches": args.steps, "cpu_baseline": cpu,
+    }), flush=True)
+
+
+def prefix_cpu(toks, cu, cub, pool):
+    """The oracle's chain hash and admission (the reference's O(trie) LRU scan)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as orc
+    t0 = time.perf_counter()
+    hashes, _ = orc.hash_chains(toks, cu, np.zeros(len(cu) - 1, dtype=np.uint64), 16)
+    m, p = orc.PagedCacheManager(16, pool), orc.PrefixCacheManager(pool)
+    orc.prefix_admit(m, p, toks, cu, hashes, cub)
+    sec = time.perf_counter() - t0
+    return 0.0, sec
 
 
 def env_int(name, default):
@@ -314,13 +441,36 @@ def main():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="decode", choices=sorted(WORKLOADS) + ["prefix"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=None,
                     help="layers in the pool (profiling runs only; a gather moves the same bytes per layer)")
     ap.add_argument("--quick", action="store_true", help="device-timed loop only (profiling runs)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    rank, world = env_int("RANK", 0), env_int("WORLD_SIZE", 1)
+    if args.workload == "prefix":
+        if args.impl == "reference":
+            if rank == 0:
+                toks, cu = prefix_requests(0x5EED + 4)
+                cub = np.zeros(len(cu), dtype=np.int64)
+                cub[1:] = np.cumsum((np.diff(cu) + 15) // 16)
+                sys.path.insert(0, os.path.join(ROOT, "oracle"))
+                import oracle as orc
+                hashes, _ = orc.hash_chains(toks, cu, np.zeros(len(cu) - 1, dtype=np.uint64), 16)
+                pool = prefix_pool_size(toks, cu, cub, hashes)
+                _, sec = prefix_cpu(toks, cu, cub, pool)
+                v = round((len(cu) - 1) / sec, 2)
+                print(json.dumps({"impl": "reference", "metric": PREFIX_METRIC, "value": v, "unit": "admissions/s",
+                                  "n_gpus": world, "steps": 1, "warmup": 0, "ms_per_step": round(sec * 1e3, 2),
+                                  "higher_is_better": True, "scaling": "replicas", "vs_baseline": None,
+                                  "dtype": "u32", "data": "synthetic", "config": {"workload": PREFIX_DESC},
+                                  "cpu_baseline": {"value": v, "unit": "admissions/s", "cores": 1, "kind": "port",
+                                                   "sample": "all 512 requests, single thread"},
+                                  "e2e": {"value": v, "unit": "admissions/s", "h2d_bytes_per_step": 0,
+                                          "d2h_bytes_per_step": 0}}), flush=True)
+            return
+        return run_prefix(args, rank, world)
     w = WORKLOADS[args.workload]
     if args.layers:
         w.layers = args.layers

@@ -173,6 +173,33 @@ RMLX_API size_t rmlx_mem_prefix_cache_memory_limit_bytes(const rmlx_mem_prefix_c
 RMLX_API size_t rmlx_mem_prefix_cache_num_blocks(const rmlx_mem_prefix_cache* p);
 
 /* ======================================================================
+ * Prefix-cache admission (host policy glue).  The reference holds a
+ * PrefixCacheManager in its scheduler but never sets it (rmlx-serve-
+ * scheduler scheduler.rs:168-172); this batched entry admits requests
+ * through a PagedCacheManager and a PrefixCacheManager with the policy
+ * described in csrc/admission.cc: per-block reuse by chain hash (see
+ * rmlx_hash_block_chains), allocation with LRU eviction from the prefix
+ * cache while the pool is empty, hash registration of new full blocks,
+ * insertion of the full-block prefix (the cache holds one reference per
+ * block it holds), then release of the request's own references.
+ * ==================================================================== */
+typedef struct rmlx_admit_stats {
+  size_t requests, admitted, rejected;
+  size_t hit_blocks, new_blocks, evictions;
+  size_t lookup_tokens;
+} rmlx_admit_stats;
+
+/* tokens[cu_tokens[r] .. cu_tokens[r+1]) are request r's token ids and
+ * hashes[cu_blocks[r] + b] its chain hashes (host arrays); cu_blocks[r+1] -
+ * cu_blocks[r] must be ceil(len / block_size).  On return block_ids[cu_blocks[r]
+ * + b] holds the block used for block b (-1 for a rejected request) and
+ * evicted[0 .. min(*n_evicted, evicted_cap)) the evicted blocks in order. */
+RMLX_API rmlx_status rmlx_prefix_admit(rmlx_block_manager* m, rmlx_prefix_cache* p, const uint32_t* tokens,
+                                       const int64_t* cu_tokens, const uint64_t* hashes, const int64_t* cu_blocks,
+                                       int32_t num_requests, int32_t* block_ids, int32_t* evicted,
+                                       size_t evicted_cap, size_t* n_evicted, rmlx_admit_stats* stats);
+
+/* ======================================================================
  * QuantizedKVCache -- quantized_cache.rs:14-296.  Same host-slice API and
  * byte layout as the reference (per layer, append-call order, groups of
  * group_size over each appended [heads, tokens, head_dim] slice); storage

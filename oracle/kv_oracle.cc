@@ -189,6 +189,14 @@ struct PrefixCache {
   }
 
   void insert(const uint32_t* tokens, size_t n, const size_t* ids, size_t nb) {  // :126-179
+    insert_report(tokens, n, ids, nb, nullptr, nullptr);
+  }
+  // insert (:126-179) that also records, per block index, whether the
+  // boundary node had no block (attached) and the block it replaced.
+  void insert_report(const uint32_t* tokens, size_t n, const size_t* ids, size_t nb, std::vector<int>* attached,
+                     std::vector<long long>* replaced) {
+    if (attached) attached->assign(nb, 0);
+    if (replaced) replaced->assign(nb, -1);
     if (n == 0 || nb == 0) return;
     size_t tpb = (nb == 1) ? n : n / nb;
     access_counter += 1;
@@ -212,9 +220,11 @@ struct PrefixCache {
       }
       if (boundary && bi < nb) {
         bool had = nodes[next].has_block;
+        if (had && replaced && nodes[next].block_id != ids[bi]) (*replaced)[bi] = (long long)nodes[next].block_id;
         nodes[next].has_block = true;
         nodes[next].block_id = ids[bi];
         if (!had) num_blocks += 1;
+        if (!had && attached) (*attached)[bi] = 1;
         bi += 1;
       }
       cur = next;
@@ -1007,6 +1017,87 @@ int orc_paged_gather_dequant(const uint8_t* pool, const int64_t* g, int64_t laye
   int e = 0;
   for (int x : errs) e |= x;
   return e;
+}
+
+// Prefix-cache admission driver (build-defined policy; the reference never
+// connects PagedCacheManager and PrefixCacheManager).  Per request: LRU touch
+// by prefix lookup of the full-block tokens; reuse of every full block whose
+// chain hash is registered (request reference); allocation of the rest with
+// LRU eviction from the prefix cache while the pool is empty (reject when
+// nothing is left to evict); token ids and hashes of new blocks; insertion
+// of the full-block prefix with one cache reference per newly held block;
+// release of the request's references.  stats: requests, admitted, rejected,
+// hit_blocks, new_blocks, evictions, lookup_tokens.
+int orc_prefix_admit(void* mv, void* pv, const uint32_t* tokens, const int64_t* cu_tokens, const uint64_t* hashes,
+                     const int64_t* cu_blocks, int64_t nreq, int64_t* block_ids, int64_t* evicted, int64_t cap,
+                     int64_t* n_evicted, int64_t* stats) {
+  auto* m = (PagedManager*)mv;
+  auto* p = (PrefixCache*)pv;
+  int64_t bs = (int64_t)m->block_size;
+  for (int i = 0; i < 7; ++i) stats[i] = 0;
+  *n_evicted = 0;
+  std::vector<int> attached;
+  std::vector<long long> replaced;
+  for (int64_t r = 0; r < nreq; ++r) {
+    int64_t n = cu_tokens[r + 1] - cu_tokens[r];
+    const uint32_t* t = tokens + cu_tokens[r];
+    const uint64_t* h = hashes + cu_blocks[r];
+    int64_t* ids = block_ids + cu_blocks[r];
+    int64_t nb = cu_blocks[r + 1] - cu_blocks[r];
+    int64_t nfull = n / bs;
+    stats[0] += 1;
+    stats[6] += nfull * bs;
+    p->lookup(t, (size_t)(nfull * bs));
+    for (int64_t b = 0; b < nb; ++b) {
+      ids[b] = -1;
+      size_t id;
+      if (b < nfull && m->lookup_hash(h[b], &id)) {
+        m->increment_ref(id);
+        ids[b] = (int64_t)id;
+        stats[3] += 1;
+      }
+    }
+    bool rejected = false;
+    for (int64_t b = 0; b < nb && !rejected; ++b) {
+      if (ids[b] >= 0) continue;
+      size_t id;
+      while (!m->allocate(&id)) {
+        size_t victim;
+        if (!p->evict_lru(&victim)) {
+          rejected = true;
+          break;
+        }
+        m->free_block(victim);
+        if (*n_evicted < cap) evicted[*n_evicted] = (int64_t)victim;
+        *n_evicted += 1;
+        stats[5] += 1;
+      }
+      if (rejected) break;
+      ids[b] = (int64_t)id;
+      stats[4] += 1;
+      int64_t cnt = (b + 1) * bs <= n ? bs : n - b * bs;
+      m->append_tokens(id, t + b * bs, (size_t)cnt);
+      if (b < nfull) m->register_hash(id, h[b]);
+    }
+    if (rejected) {
+      for (int64_t b = 0; b < nb; ++b)
+        if (ids[b] >= 0) m->free_block((size_t)ids[b]);
+      for (int64_t b = 0; b < nb; ++b) ids[b] = -1;
+      stats[2] += 1;
+      continue;
+    }
+    if (nfull > 0) {
+      std::vector<size_t> full(ids, ids + nfull);
+      p->insert_report(t, (size_t)(nfull * bs), full.data(), (size_t)nfull, &attached, &replaced);
+      for (int64_t b = 0; b < nfull; ++b) {
+        if (attached[b]) m->increment_ref((size_t)ids[b]);
+        if (replaced[b] >= 0) m->free_block((size_t)replaced[b]);
+      }
+    }
+    for (int64_t b = 0; b < nb; ++b) m->free_block((size_t)ids[b]);
+    stats[1] += 1;
+  }
+  return ORC_OK;
 }
 
 // Element conversions used by tests (RNE, same as the reference's f32 path

@@ -102,6 +102,7 @@ _sig("orc_paged_append_quant", C.c_int, vp, i64p, C.c_int64, C.c_int64, vp, vp, 
      C.c_int64, i64p, C.c_int64)
 _sig("orc_paged_gather_dequant", C.c_int, vp, i64p, C.c_int64, i32p, C.c_int64, i32p, C.c_int64, vp, vp, C.c_int,
      C.c_int)
+_sig("orc_prefix_admit", C.c_int, vp, vp, u32p, i64p, u64p, i64p, C.c_int64, i64p, i64p, C.c_int64, i64p, i64p)
 _sig("orc_f32_to_dtype", None, f32p, vp, C.c_int64, C.c_int)
 _sig("orc_dtype_to_f32", None, vp, f32p, C.c_int64, C.c_int)
 
@@ -364,6 +365,25 @@ class RotatingKVCache:
 
     def trim(self, n):
         _chk(_l.orc_rot_trim(self._h, n))
+
+
+STAT_NAMES = ("requests", "admitted", "rejected", "hit_blocks", "new_blocks", "evictions", "lookup_tokens")
+
+
+def prefix_admit(mgr: "PagedCacheManager", prefix: "PrefixCacheManager", tokens, cu_tokens, hashes, cu_blocks):
+    """Admission policy restated (see kv_oracle.cc): (block_ids, evicted, stats)."""
+    t = _a(tokens, np.uint32) if len(tokens) else np.zeros(1, np.uint32)
+    cu, cub = _a(cu_tokens, np.int64), _a(cu_blocks, np.int64)
+    hs = _a(hashes, np.uint64) if len(hashes) else np.zeros(1, np.uint64)
+    nreq = len(cu) - 1
+    ids = np.zeros(max(int(cub[-1]), 1), dtype=np.int64)
+    cap = int(cub[-1]) * 4 + 16
+    ev = np.zeros(cap, dtype=np.int64)
+    nev = C.c_int64()
+    st = np.zeros(7, dtype=np.int64)
+    _chk(_l.orc_prefix_admit(mgr._h, prefix._h, _p(t, u32p), _p(cu, i64p), _p(hs, u64p), _p(cub, i64p), nreq,
+                             _p(ids, i64p), _p(ev, i64p), cap, C.byref(nev), _p(st, i64p)))
+    return ids[:int(cub[-1])], ev[:min(nev.value, cap)], dict(zip(STAT_NAMES, st.tolist())), nev.value
 
 
 def xxh64(data: bytes, seed: int = 0) -> int:

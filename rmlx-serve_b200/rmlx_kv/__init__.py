@@ -5,8 +5,8 @@ the rmlx-serve-cache crate (crates/rmlx-serve-cache/src/lib.rs:30-40).
 """
 from ._lib import BF16, F16, F32, RmlxError, LIB_PATH  # noqa: F401
 from .cache import (KVCacheBlock, MemoryAwarePrefixCache, PagedCacheManager,  # noqa: F401
-                    PrefixCacheManager, QuantizedKVCache)
+                    PrefixCacheManager, QuantizedKVCache, prefix_admit)
 from .pool import KVPool, NcclComm, hash_block_chains  # noqa: F401
 
 __all__ = ["KVCacheBlock", "PagedCacheManager", "PrefixCacheManager", "MemoryAwarePrefixCache",
-           "QuantizedKVCache", "KVPool", "NcclComm", "hash_block_chains", "RmlxError", "F32", "F16", "BF16"]
+           "QuantizedKVCache", "prefix_admit", "KVPool", "NcclComm", "hash_block_chains", "RmlxError", "F32", "F16", "BF16"]

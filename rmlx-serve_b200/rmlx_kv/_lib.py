@@ -51,6 +51,11 @@ class BlockView(C.Structure):
                 ("hash", C.c_uint64), ("num_filled", C.c_size_t)]
 
 
+class AdmitStats(C.Structure):
+    _fields_ = [(n, C.c_size_t) for n in (
+        "requests", "admitted", "rejected", "hit_blocks", "new_blocks", "evictions", "lookup_tokens")]
+
+
 class PoolConfig(C.Structure):
     _fields_ = [(n, C.c_int32) for n in (
         "num_layers", "num_kv_heads", "head_dim", "block_size", "num_blocks", "dtype",
@@ -117,6 +122,10 @@ _sig("rmlx_mem_prefix_cache_hit_rate", C.c_double, vp)
 _sig("rmlx_mem_prefix_cache_current_usage_bytes", C.c_size_t, vp)
 _sig("rmlx_mem_prefix_cache_memory_limit_bytes", C.c_size_t, vp)
 _sig("rmlx_mem_prefix_cache_num_blocks", C.c_size_t, vp)
+
+# admission
+_sig("rmlx_prefix_admit", st, vp, vp, u32p, i64p, u64p, i64p, C.c_int32, i32p, i32p, C.c_size_t, c_size_p,
+     C.POINTER(AdmitStats))
 
 # QuantizedKVCache
 _sig("rmlx_qcache_new", st, C.c_size_t, C.c_size_t, C.c_size_t, C.c_size_t, C.c_size_t, C.c_int,

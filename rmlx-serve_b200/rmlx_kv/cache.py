@@ -302,3 +302,26 @@ class QuantizedKVCache:
 
     def group_size(self) -> int:
         return lib.rmlx_qcache_group_size(self._h)
+
+
+def prefix_admit(mgr: PagedCacheManager, prefix: PrefixCacheManager, tokens, cu_tokens, hashes, cu_blocks):
+    """Admit requests in order through `mgr` and `prefix` (rmlx_prefix_admit).
+
+    Returns (block_ids per block, evicted block ids in order, stats dict).
+    """
+    t = np.ascontiguousarray(np.asarray(tokens, dtype=np.uint32)) if len(tokens) else np.zeros(1, np.uint32)
+    cu = np.ascontiguousarray(np.asarray(cu_tokens, dtype=np.int64))
+    cub = np.ascontiguousarray(np.asarray(cu_blocks, dtype=np.int64))
+    hs = np.ascontiguousarray(np.asarray(hashes, dtype=np.uint64)) if len(hashes) else np.zeros(1, np.uint64)
+    nblk = int(cub[-1])
+    ids = np.zeros(max(nblk, 1), dtype=np.int32)
+    cap = 4 * nblk + 16
+    ev = np.zeros(cap, dtype=np.int32)
+    nev = C.c_size_t()
+    stats = _lib.AdmitStats()
+    check(lib.rmlx_prefix_admit(mgr._h, prefix._h, t.ctypes.data_as(_lib.u32p), cu.ctypes.data_as(_lib.i64p),
+                                hs.ctypes.data_as(_lib.u64p), cub.ctypes.data_as(_lib.i64p), len(cu) - 1,
+                                ids.ctypes.data_as(_lib.i32p), ev.ctypes.data_as(_lib.i32p), cap, C.byref(nev),
+                                C.byref(stats)))
+    st = {n: getattr(stats, n) for n, _ in _lib.AdmitStats._fields_}
+    return ids[:nblk], ev[:min(nev.value, cap)], st

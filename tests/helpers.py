@@ -52,3 +52,24 @@ def to_dev(a, device="cuda"):
 
 def to_host(t, dtype):
     return t.cpu().numpy().view(dtype)
+
+
+def prefix_workload(rng, n_req, n_prefix, prefix_len, suffix_range, unique_range, vocab=128256, shared=0.6):
+    """Requests for the prefix-caching workload: a fraction `shared` start with
+    one of `n_prefix` shared prefixes of `prefix_len` tokens plus a unique
+    suffix (length uniform in suffix_range), the rest are unique (length
+    uniform in unique_range).  Token ids uniform over `vocab`.
+    Returns (tokens uint32, cu_tokens int64)."""
+    prefixes = [rng.integers(0, vocab, size=prefix_len, dtype=np.uint32) for _ in range(n_prefix)]
+    reqs = []
+    for _ in range(n_req):
+        if rng.random() < shared:
+            p = prefixes[int(rng.integers(n_prefix))]
+            suf = rng.integers(0, vocab, size=int(rng.integers(suffix_range[0], suffix_range[1] + 1)), dtype=np.uint32)
+            reqs.append(np.concatenate([p, suf]))
+        else:
+            reqs.append(rng.integers(0, vocab, size=int(rng.integers(unique_range[0], unique_range[1] + 1)),
+                                     dtype=np.uint32))
+    cu = np.zeros(n_req + 1, dtype=np.int64)
+    cu[1:] = np.cumsum([len(r) for r in reqs])
+    return np.concatenate(reqs).astype(np.uint32), cu

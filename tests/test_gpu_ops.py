@@ -166,3 +166,16 @@ def test_qcache_length_mismatch(cuda):
     c = rmlx_kv.QuantizedKVCache(1, 2, 8, 8, 8)
     with pytest.raises(rmlx_kv.RmlxError, match="length mismatch"):
         c.append(0, np.zeros(8, np.float32), np.zeros(8, np.float32), 1)
+
+
+def test_chain_hash_full_prefix_workload(cuda):
+    """All blocks of the prefix-caching workload (512 requests, ~640k tokens)."""
+    import torch
+    from helpers import prefix_workload
+    rng = np.random.default_rng(0x5EED + 4)
+    toks, cu = prefix_workload(rng, 512, 8, 1024, (64, 512), (256, 2048))
+    roots = np.zeros(512, dtype=np.uint64)
+    want, cub = orc.hash_chains(toks, cu, roots, 16)
+    out = torch.zeros(len(want), dtype=torch.int64, device=cuda)
+    rmlx_kv.hash_block_chains(to_dev(toks), to_dev(cu), None, 512, 16, to_dev(cub), out)
+    np.testing.assert_array_equal(out.cpu().numpy().view(np.uint64), want)
