@@ -1,0 +1,92 @@
+"""Block tables of a decode batch with forked sequences (beam / speculative
+branches), kept over a block manager.
+
+A fork makes the child share every block of the parent: the child's old
+blocks are released (paged_cache.rs:125-149, free) and each of the
+parent's gains a reference (paged_cache.rs:172-182, increment_ref).  The
+next token appended to a sequence whose tail block is shared goes through
+copy_on_write (paged_cache.rs:197-224): the manager hands out a private block, and the
+device must copy the shared tile into it (``KVPool.copy_blocks``) before
+the token is written.  ``append_slots`` returns those copy pairs together
+with the slot of each sequence's new token, so one step is
+
+    copy_blocks(cow_src, cow_dst) -> append(slots) -> gather(block_table)
+
+The manager is any object with the reference's allocate / free /
+increment_ref / copy_on_write methods (this package's PagedCacheManager,
+or the oracle's restatement in the tests).
+"""
+from __future__ import annotations
+
+from typing import List, Sequence, Tuple
+
+import numpy as np
+
+
+class PoolExhausted(RuntimeError):
+    pass
+
+
+class SequenceBlocks:
+    def __init__(self, mgr, block_size: int, lens: Sequence[int]):
+        self.mgr = mgr
+        self.bs = int(block_size)
+        self.lens = [int(x) for x in lens]
+        self.tables: List[List[int]] = [[self._alloc() for _ in range((n + self.bs - 1) // self.bs)]
+                                        for n in self.lens]
+
+    def _alloc(self) -> int:
+        bid = self.mgr.allocate()
+        if bid is None:
+            raise PoolExhausted("no free block")
+        return int(bid)
+
+    def release(self, seq: int) -> None:
+        """Drop the sequence's references (its blocks return to the free list
+        when no other sequence holds them)."""
+        for b in self.tables[seq]:
+            self.mgr.free(b)
+        self.tables[seq] = []
+        self.lens[seq] = 0
+
+    def fork(self, parent: int, child: int) -> None:
+        """Replace `child` by a branch of `parent` that shares all its blocks."""
+        if parent == child:
+            return
+        self.release(child)
+        for b in self.tables[parent]:
+            self.mgr.increment_ref(b)
+        self.tables[child] = list(self.tables[parent])
+        self.lens[child] = self.lens[parent]
+
+    def append_slots(self) -> Tuple[np.ndarray, np.ndarray, np.ndarray]:
+        """One new token per sequence.  Returns (cow_src, cow_dst, slots):
+        the tiles to copy before the append and each token's pool slot
+        (block * block_size + offset)."""
+        src, dst = [], []
+        slots = np.empty(len(self.lens), dtype=np.int32)
+        for s, pos in enumerate(self.lens):
+            t = self.tables[s]
+            bi = pos // self.bs
+            if bi == len(t):
+                t.append(self._alloc())
+            else:
+                nid = self.mgr.copy_on_write(t[bi])
+                if nid is not None:
+                    src.append(t[bi])
+                    dst.append(int(nid))
+                    t[bi] = int(nid)
+            slots[s] = t[bi] * self.bs + pos % self.bs
+            self.lens[s] = pos + 1
+        return np.array(src, dtype=np.int32), np.array(dst, dtype=np.int32), slots
+
+    def block_table(self) -> np.ndarray:
+        """[num_seqs, max blocks] int32, rows padded with 0."""
+        width = max([len(t) for t in self.tables] + [1])
+        bt = np.zeros((len(self.tables), width), dtype=np.int32)
+        for s, t in enumerate(self.tables):
+            bt[s, :len(t)] = t
+        return bt
+
+    def seq_lens(self) -> np.ndarray:
+        return np.array(self.lens, dtype=np.int32)
