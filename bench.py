@@ -78,7 +78,7 @@ class Workload:
 
     @property
     def kernel(self):
-        return "gather_dequant_kernel" if self.bits else "gather_rows_kernel"
+        return "gather_dequant_r1_kernel" if self.bits else "gather_rows_kernel"
 
     @property
     def profile(self):

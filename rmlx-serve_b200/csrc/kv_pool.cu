@@ -364,11 +364,18 @@ __global__ void __launch_bounds__(256) append_quant_kernel(PoolGeo g, int l0, in
 // Dequantise-on-gather.
 //
 // Per element the reference computes (code as f32) * scale + zero with a
-// rounded multiply then a rounded add (dequantize_group); the kernel keeps
-// exactly that (__fmul_rn, __fadd_rn).  It avoids the slow conversion pipe
-// for the code: a byte permute builds the f32 bit pattern of 2^23 + code
-// (exact for codes < 2^23) and an exact subtraction of 2^23 recovers
-// (float)code.
+// rounded multiply then a rounded add (dequantize_group).  The code's f32
+// value comes from a byte permute that builds the bit pattern of 2^23 + code
+// (exact for codes < 2^23) and an exact subtraction of 2^23, which keeps the
+// slow conversion pipe out of the loop.  Then:
+//  * f32 scale/zero: a rounded multiply and a rounded add (__fmul_rn,
+//    __fadd_rn), exactly the reference's two steps;
+//  * f16 scale/zero: code * scale is exact in f32 (a code has at most 8
+//    significant bits and an f16 value 11, and the product stays inside
+//    f32's normal range), so a fused multiply-add, which rounds once after
+//    the add, gives the same result as the reference's multiply then add.
+//    The kernel uses the packed forms (add.rn.f32x2, fma.rn.f32x2): one
+//    instruction for two elements.
 //
 // Layout of the work: persistent CTAs, one warp per (sequence block, kv,
 // head) tile.  A lane's task is one 16-byte segment of output (8 bf16/f16
@@ -377,11 +384,61 @@ __global__ void __launch_bounds__(256) append_quant_kernel(PoolGeo g, int l0, in
 // bytes) and read consecutive code bytes.  group_size >= 8 and a power of
 // two, so a task never straddles a (scale, zero) group.  All of a round's
 // loads (codes and scale/zero) are issued before its first store.
+//
+// Task indexing (IDX): with tpr tasks per row, a task's row and group are
+// found by division (0: tpr not a power of two), by shifts (1), or, when
+// tpr divides 32 (2: the common head_dim 128 with 16-bit output), from
+// per-lane constants: a lane's group is the same in every round step and
+// its row advances by 32 / tpr rows per step.
 // ---------------------------------------------------------------------------
 
-// f32 value of byte `b` of `w`, via the bit pattern of 2^23 + byte.
-__device__ __forceinline__ float code_byte(uint32_t w, int b) {
-  return __fadd_rn(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440u | (uint32_t)b)), -8388608.0f);
+// f32 bit pattern of 2^23 + byte `b` of `w`.
+__device__ __forceinline__ float magic_byte(uint32_t w, int b) {
+  return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440u | (uint32_t)b));
+}
+
+// Two f32 values in one 64-bit register, for the packed f32x2 instructions.
+__device__ __forceinline__ uint64_t f32x2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1,%2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f32x2_split(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0,%1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t add_f32x2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
+// Dequantised elements e and e + 1 (e even) of a task.  8-bit: bytes of the
+// task's code words; 4-bit: the low and high nibble of byte e / 2, taken
+// from the pre-masked words lo4 (low nibbles) and hi4 (high nibbles).
+template <int BITS, bool META_F32>
+__device__ __forceinline__ void dq_pair(const uint2& cw, uint32_t lo4, uint32_t hi4, int e, float sc, float zr,
+                                        float& a, float& b) {
+  float m0, m1;
+  if (BITS == 8) {
+    const uint32_t w = e < 4 ? cw.x : cw.y;
+    m0 = magic_byte(w, e & 3);
+    m1 = magic_byte(w, (e + 1) & 3);
+  } else {
+    m0 = magic_byte(lo4, e >> 1);
+    m1 = magic_byte(hi4, e >> 1);
+  }
+  if (META_F32) {
+    a = __fadd_rn(__fmul_rn(__fadd_rn(m0, -8388608.0f), sc), zr);
+    b = __fadd_rn(__fmul_rn(__fadd_rn(m1, -8388608.0f), sc), zr);
+  } else {
+    const uint64_t q = add_f32x2(f32x2(m0, m1), f32x2(-8388608.0f, -8388608.0f));
+    f32x2_split(fma_f32x2(q, f32x2(sc, sc), f32x2(zr, zr)), a, b);
+  }
 }
 
 template <bool META_F32>
@@ -438,57 +495,192 @@ struct Store16<RMLX_BF16> {
 // each tile.  All loads (codes, scale/zero) are issued before the first store.
 // Task t reads code bytes [t * CB, (t + 1) * CB) (code rows are contiguous)
 // and writes output bytes [16 t, 16 t + 16) (the tile's output rows are
-// contiguous too).
-template <int BITS, int OUT_DT, bool META_F32, bool POW2, int TPW, int V>
+// contiguous too).  base is a multiple of 32 * V.
+template <int BITS, int OUT_DT, bool META_F32, int IDX, int TPW, int V>
 __device__ __forceinline__ void dq_round(const PoolGeo& g, const uint8_t* const* tile, uint8_t* const* out,
                                          const int* ntasks, int base, int lane, int tpr, int tpr_log2, int gs_log2) {
   constexpr int EPT = Store16<OUT_DT>::n;  // output elements per task (16 bytes)
   constexpr int CB = EPT * BITS / 8;       // code bytes per task
+  constexpr int MSZ = META_F32 ? 8 : 4;    // bytes of one (scale, zero) pair
   const int meta_off = g.bs * g.row_bytes;
+  const int mrb = g.meta_row_bytes;
+  const int t0 = base + lane;
+  // IDX 2: byte offset of this lane's (scale, zero) in the tile at v = 0,
+  // and its advance per v.
+  int moff = 0, mstep = 0;
+  if (IDX == 2) {
+    moff = meta_off + (t0 >> tpr_log2) * mrb + (((lane & (tpr - 1)) * EPT) >> gs_log2) * MSZ;
+    mstep = (32 >> tpr_log2) * mrb;
+  }
   uint2 cw[TPW][V];
   float sc[TPW][V], zr[TPW][V];
 #pragma unroll
-  for (int k = 0; k < TPW; ++k)
+  for (int k = 0; k < TPW; ++k) {
+    const uint8_t* cbase = tile[k] + t0 * CB;
+    const uint8_t* mbase = tile[k] + moff;
 #pragma unroll
     for (int v = 0; v < V; ++v) {
-      const int t = base + lane + 32 * v;
+      const int t = t0 + 32 * v;
       cw[k][v] = make_uint2(0u, 0u);
       sc[k][v] = zr[k][v] = 0.0f;
       if (t < ntasks[k]) {
-        cw[k][v] = load_codes<CB>(tile[k] + t * CB);
-        const int r = POW2 ? (t >> tpr_log2) : t / tpr;
-        const int e0 = (POW2 ? (t & (tpr - 1)) : (t - r * tpr)) * EPT;
-        meta_at<META_F32>(tile[k] + meta_off + r * g.meta_row_bytes, e0 >> gs_log2, sc[k][v], zr[k][v]);
+        cw[k][v] = load_codes<CB>(cbase + 32 * CB * v);
+        if (IDX == 2) {
+          meta_at<META_F32>(mbase + v * mstep, 0, sc[k][v], zr[k][v]);
+        } else {
+          const int r = IDX ? (t >> tpr_log2) : t / tpr;
+          const int e0 = (IDX ? (t & (tpr - 1)) : (t - r * tpr)) * EPT;
+          meta_at<META_F32>(tile[k] + meta_off + r * mrb, e0 >> gs_log2, sc[k][v], zr[k][v]);
+        }
       }
     }
+  }
 #pragma unroll
-  for (int k = 0; k < TPW; ++k)
+  for (int k = 0; k < TPW; ++k) {
+    uint8_t* obase = out[k] + (int64_t)t0 * 16;
 #pragma unroll
     for (int v = 0; v < V; ++v) {
-      const int t = base + lane + 32 * v;
-      if (t >= ntasks[k]) continue;
-      float f[EPT];
-#pragma unroll
-      for (int e = 0; e < EPT; ++e) {
-        float qv;
-        if (BITS == 8) {
-          qv = code_byte(e < 4 ? cw[k][v].x : cw[k][v].y, e & 3);
-        } else {  // element e is nibble e: the low nibble of byte e/2 for even e
-          const uint32_t w = cw[k][v].x;
-          qv = code_byte((e & 1) ? ((w >> 4) & 0x0F0F0F0Fu) : (w & 0x0F0F0F0Fu), e >> 1);
-        }
-        f[e] = __fadd_rn(__fmul_rn(qv, sc[k][v]), zr[k][v]);
+      if (t0 + 32 * v >= ntasks[k]) continue;
+      uint32_t lo4 = 0, hi4 = 0;
+      if (BITS == 4) {
+        lo4 = cw[k][v].x & 0x0F0F0F0Fu;
+        hi4 = (cw[k][v].x >> 4) & 0x0F0F0F0Fu;
       }
-      Store16<OUT_DT>::run(out[k] + (int64_t)t * 16, f);
+      if (OUT_DT == RMLX_F32) {
+        float f[4];
+        dq_pair<BITS, META_F32>(cw[k][v], lo4, hi4, 0, sc[k][v], zr[k][v], f[0], f[1]);
+        dq_pair<BITS, META_F32>(cw[k][v], lo4, hi4, 2, sc[k][v], zr[k][v], f[2], f[3]);
+        Store16<RMLX_F32>::run(obase + 512 * v, f);
+      } else {  // 16-bit output: each pair packed as soon as it is computed
+        uint32_t w[4];
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          float a, b;
+          dq_pair<BITS, META_F32>(cw[k][v], lo4, hi4, 2 * p, sc[k][v], zr[k][v], a, b);
+          w[p] = Elem<OUT_DT == RMLX_F32 ? RMLX_BF16 : OUT_DT>::pack(a, b);
+        }
+        st_stream(obase + 512 * v, make_uint4(w[0], w[1], w[2], w[3]));
+      }
     }
+  }
 }
 
-// Persistent CTAs, two CTAs of 256 threads per SM; each warp dequantises
-// two tiles per round.  POW2: head_dim / EPT is a power of two (2^tpr_log2)
-// and a task's row is found by a shift, else by division.  A tile with at
-// most 32 * V tasks (every 16 x 128 bf16/f16 tile) takes one round with a
-// compile-time base of 0.
-template <int BITS, int OUT_DT, bool META_F32, bool POW2>
+// The common case as its own kernel: every tile fits one round (block_size *
+// tasks per row <= 32 * V) and tasks per row divide 32, so a lane's code,
+// (scale, zero) and output addresses are per-lane constants plus immediate
+// offsets.  Same tasks, loads and arithmetic as gather_dequant_kernel.
+template <int BITS, int OUT_DT, bool META_F32>
+__global__ void __launch_bounds__(256, 2) gather_dequant_r1_kernel(PoolGeo g, int layer, const int32_t* __restrict__ bt,
+                                                                   int bt_stride, const int32_t* __restrict__ lens,
+                                                                   int nseq, uint8_t* __restrict__ ok,
+                                                                   uint8_t* __restrict__ ov, int hd, int gs_log2,
+                                                                   int tpr_log2, int32_t* err) {
+  constexpr int EPT = Store16<OUT_DT>::n;
+  constexpr int CB = EPT * BITS / 8;
+  constexpr int MSZ = META_F32 ? 8 : 4;
+  constexpr int V = 8, TPW = 2;
+  extern __shared__ int32_t smem[];
+  int32_t* cub = smem;
+  int32_t* cut = smem + nseq + 1;
+  pdl_wait();
+  pdl_release();
+  scan_seq_lens(lens, nseq, g.bs, cub, cut);
+  const int64_t units = (int64_t)cub[nseq] * 2 * g.heads;
+  const bool units32 = units <= (int64_t)UINT32_MAX;
+  const int lane = threadIdx.x & 31;
+  const int tpr = 1 << tpr_log2;
+  const int mrb = g.meta_row_bytes;
+  const int64_t orb = (int64_t)hd * (16 / EPT);
+  // per-lane constants: code offset, (scale, zero) offset and its advance per v
+  const int coff = lane * CB;
+  const int moff = g.bs * g.row_bytes + (lane >> tpr_log2) * mrb + (((lane & (tpr - 1)) * EPT) >> gs_log2) * MSZ;
+  const int mstep = (32 >> tpr_log2) * mrb;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t u0 = ((blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5) * TPW; u0 < units;
+       u0 += nwarps * TPW) {
+    const uint8_t* tile[TPW];
+    uint8_t* out[TPW];
+    int ntasks[TPW];
+#pragma unroll
+    for (int k = 0; k < TPW; ++k) {
+      const int64_t u = u0 + k;
+      tile[k] = g.base;
+      out[k] = ok;
+      ntasks[k] = 0;
+      if (u >= units) continue;
+      int h, kv;
+      int64_t gi;
+      if (units32) {
+        const uint32_t uu = (uint32_t)u, hh = (uint32_t)g.heads, q = uu / hh;
+        h = (int)(uu - q * hh);
+        kv = (int)(q & 1u);
+        gi = (int64_t)(q >> 1);
+      } else {
+        h = (int)(u % g.heads);
+        const int64_t q = u / g.heads;
+        kv = (int)(q & 1);
+        gi = q >> 1;
+      }
+      const int s = find_seq(cub, nseq, gi);
+      const int b = (int)(gi - cub[s]);
+      const int L = cut[s + 1] - cut[s];
+      const int32_t blk = __ldg(bt + (int64_t)s * bt_stride + b);
+      if (blk < 0 || blk >= g.nblocks) {
+        if (lane == 0) atomicOr(err, DEV_ERR_BLOCK);
+        continue;
+      }
+      tile[k] = g.base + g.tile_off(blk, layer, kv, h);
+      out[k] = (kv ? ov : ok) + ((int64_t)cut[s] * g.heads + (int64_t)h * L + (int64_t)b * g.bs) * orb;
+      ntasks[k] = min(g.bs, L - b * g.bs) << tpr_log2;
+    }
+    uint2 cw[TPW][V];
+    float sc[TPW][V], zr[TPW][V];
+#pragma unroll
+    for (int k = 0; k < TPW; ++k) {
+      const uint8_t* cbase = tile[k] + coff;
+      const uint8_t* mbase = tile[k] + moff;
+#pragma unroll
+      for (int v = 0; v < V; ++v) {
+        cw[k][v] = make_uint2(0u, 0u);
+        sc[k][v] = zr[k][v] = 0.0f;
+        if (lane + 32 * v < ntasks[k]) {
+          cw[k][v] = load_codes<CB>(cbase + 32 * CB * v);
+          meta_at<META_F32>(mbase + v * mstep, 0, sc[k][v], zr[k][v]);
+        }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < TPW; ++k) {
+      uint8_t* obase = out[k] + lane * 16;
+#pragma unroll
+      for (int v = 0; v < V; ++v) {
+        if (lane + 32 * v >= ntasks[k]) continue;
+        uint32_t lo4 = 0, hi4 = 0;
+        if (BITS == 4) {
+          lo4 = cw[k][v].x & 0x0F0F0F0Fu;
+          hi4 = (cw[k][v].x >> 4) & 0x0F0F0F0Fu;
+        }
+        if (OUT_DT == RMLX_F32) {
+          float f[4];
+          dq_pair<BITS, META_F32>(cw[k][v], lo4, hi4, 0, sc[k][v], zr[k][v], f[0], f[1]);
+          dq_pair<BITS, META_F32>(cw[k][v], lo4, hi4, 2, sc[k][v], zr[k][v], f[2], f[3]);
+          Store16<RMLX_F32>::run(obase + 512 * v, f);
+        } else {
+          uint32_t w[4];
+#pragma unroll
+          for (int p = 0; p < 4; ++p) {
+            float a, b;
+            dq_pair<BITS, META_F32>(cw[k][v], lo4, hi4, 2 * p, sc[k][v], zr[k][v], a, b);
+            w[p] = Elem<OUT_DT == RMLX_F32 ? RMLX_BF16 : OUT_DT>::pack(a, b);
+          }
+          st_stream(obase + 512 * v, make_uint4(w[0], w[1], w[2], w[3]));
+        }
+      }
+    }
+  }
+}
+
+template <int BITS, int OUT_DT, bool META_F32, int IDX>
 __global__ void __launch_bounds__(256, 2) gather_dequant_kernel(PoolGeo g, int layer, const int32_t* __restrict__ bt,
                                                                 int bt_stride, const int32_t* __restrict__ lens,
                                                                 int nseq, uint8_t* __restrict__ ok,
@@ -504,6 +696,7 @@ __global__ void __launch_bounds__(256, 2) gather_dequant_kernel(PoolGeo g, int l
   pdl_release();
   scan_seq_lens(lens, nseq, g.bs, cub, cut);
   const int64_t units = (int64_t)cub[nseq] * 2 * g.heads;
+  const bool units32 = units <= (int64_t)UINT32_MAX;  // uniform: 32-bit unit arithmetic
   const int lane = threadIdx.x & 31;
   const int tpr = hd / EPT;  // tasks per row
   const int64_t orb = (int64_t)hd * (16 / EPT);
@@ -521,10 +714,20 @@ __global__ void __launch_bounds__(256, 2) gather_dequant_kernel(PoolGeo g, int l
       out[k] = nullptr;
       ntasks[k] = 0;
       if (u >= units) continue;
-      const int h = (int)(u % g.heads);
-      const int64_t q = u / g.heads;
-      const int kv = (int)(q & 1);
-      const int64_t gi = q >> 1;
+      // unit u = (gathered block gi, kv, head h), head fastest
+      int h, kv;
+      int64_t gi;
+      if (units32) {
+        const uint32_t uu = (uint32_t)u, hh = (uint32_t)g.heads, q = uu / hh;
+        h = (int)(uu - q * hh);
+        kv = (int)(q & 1u);
+        gi = (int64_t)(q >> 1);
+      } else {
+        h = (int)(u % g.heads);
+        const int64_t q = u / g.heads;
+        kv = (int)(q & 1);
+        gi = q >> 1;
+      }
       const int s = find_seq(cub, nseq, gi);
       const int b = (int)(gi - cub[s]);
       const int L = cut[s + 1] - cut[s];
@@ -539,10 +742,10 @@ __global__ void __launch_bounds__(256, 2) gather_dequant_kernel(PoolGeo g, int l
       nmax = max(nmax, ntasks[k]);
     }
     if (nmax <= 32 * V) {
-      dq_round<BITS, OUT_DT, META_F32, POW2, TPW, V>(g, tile, out, ntasks, 0, lane, tpr, tpr_log2, gs_log2);
+      dq_round<BITS, OUT_DT, META_F32, IDX, TPW, V>(g, tile, out, ntasks, 0, lane, tpr, tpr_log2, gs_log2);
     } else {
       for (int base = 0; base < nmax; base += 32 * V)
-        dq_round<BITS, OUT_DT, META_F32, POW2, TPW, V>(g, tile, out, ntasks, base, lane, tpr, tpr_log2, gs_log2);
+        dq_round<BITS, OUT_DT, META_F32, IDX, TPW, V>(g, tile, out, ntasks, base, lane, tpr, tpr_log2, gs_log2);
     }
   }
 }
@@ -673,18 +876,34 @@ AppendQuantFn pick_append_quant(int in_dt, int bits, bool mf32) {
 
 using GatherDqFn = void (*)(PoolGeo, int, const int32_t*, int, const int32_t*, int, uint8_t*, uint8_t*, int, int,
                             int, int32_t*);
-template <int BITS, int OUT, bool MF32, bool POW2>
+template <int BITS, int OUT, bool MF32, int IDX>
 GatherDqFn gd() {
-  return gather_dequant_kernel<BITS, OUT, MF32, POW2>;
+  return gather_dequant_kernel<BITS, OUT, MF32, IDX>;
 }
-GatherDqFn pick_gather_dequant(int bits, int out_dt, bool mf32, bool pow2) {
-#define GD_ROW(B, O) {{gd<B, O, false, false>(), gd<B, O, false, true>()}, {gd<B, O, true, false>(), gd<B, O, true, true>()}}
-  static const GatherDqFn t[2][3][2][2] = {
+template <int BITS, int OUT, bool MF32>
+GatherDqFn gd1() {
+  return gather_dequant_r1_kernel<BITS, OUT, MF32>;
+}
+GatherDqFn pick_gather_dequant_r1(int bits, int out_dt, bool mf32) {
+#define GD1_ROW(B, O) {gd1<B, O, false>(), gd1<B, O, true>()}
+  static const GatherDqFn t[2][3][2] = {
+      {GD1_ROW(4, 0), GD1_ROW(4, 1), GD1_ROW(4, 2)},
+      {GD1_ROW(8, 0), GD1_ROW(8, 1), GD1_ROW(8, 2)},
+  };
+#undef GD1_ROW
+  return t[bits == 8][out_dt][mf32];
+}
+// idx: 0 = tpr not a power of two, 1 = power of two above 32, 2 = divides 32
+GatherDqFn pick_gather_dequant(int bits, int out_dt, bool mf32, int idx) {
+#define GD_M(B, O, M) {gd<B, O, M, 0>(), gd<B, O, M, 1>(), gd<B, O, M, 2>()}
+#define GD_ROW(B, O) {GD_M(B, O, false), GD_M(B, O, true)}
+  static const GatherDqFn t[2][3][2][3] = {
       {GD_ROW(4, 0), GD_ROW(4, 1), GD_ROW(4, 2)},
       {GD_ROW(8, 0), GD_ROW(8, 1), GD_ROW(8, 2)},
   };
 #undef GD_ROW
-  return t[bits == 8][out_dt][mf32][pow2];
+#undef GD_M
+  return t[bits == 8][out_dt][mf32][idx];
 }
 
 }  // namespace
@@ -859,7 +1078,10 @@ rmlx_status rmlx_kv_gather(rmlx_kv_pool* p, int32_t layer, const int32_t* bt, in
   } else {
     const int ept = c.dtype == RMLX_F32 ? 4 : 8;  // output elements per 16-byte task
     const int tpr = c.head_dim / ept;
-    GatherDqFn fn = pick_gather_dequant(c.quant_bits, c.dtype, c.meta_dtype == RMLX_F32, is_pow2(tpr));
+    const int idx = !is_pow2(tpr) ? 0 : (tpr <= 32 ? 2 : 1);
+    const bool one_round = idx == 2 && (int64_t)c.block_size * tpr <= 256;  // 32 lanes x 8 tasks
+    GatherDqFn fn = one_round ? pick_gather_dequant_r1(c.quant_bits, c.dtype, c.meta_dtype == RMLX_F32)
+                              : pick_gather_dequant(c.quant_bits, c.dtype, c.meta_dtype == RMLX_F32, idx);
     if (fresh) {
       if ((s = prepare_smem(fn, smem)) != RMLX_OK) return s;
       p->gather_grid = persistent_grid(fn, 256, smem, p->num_sms);

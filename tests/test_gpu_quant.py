@@ -120,3 +120,25 @@ def test_f16_meta_error_bound(cuda):
     err16 = np.abs(outs[orc.F16] - x).max()
     # 8-bit: |error| <= scale/2 + bf16 rounding; scale <= (range)/255 with range ~ <= 2*8*4.5
     assert err32 < 0.25 and err16 < 0.3
+
+
+# (head_dim, block_size, out dtype, group): every dequant kernel path.
+#  r1 = single-round kernel (tasks per row a power of two <= 32, block_size * tasks <= 256);
+#  the general kernel: multi-round, shift indexing (tasks per row > 32), division (not a power of two).
+DISPATCH = [
+    (128, 16, orc.BF16, 64),   # r1
+    (64, 8, orc.F32, 32),      # r1, f32 output
+    (128, 32, orc.BF16, 64),   # general, 2 rounds per tile
+    (128, 16, orc.F32, 64),    # general, f32 output, 2 rounds
+    (512, 16, orc.BF16, 128),  # general, 64 tasks per row (shifts)
+    (96, 16, orc.F16, 32),     # general, 12 tasks per row (division)
+    (96, 4, orc.BF16, 32),     # general, division, short blocks
+]
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+@pytest.mark.parametrize("meta", [orc.F16, orc.F32])
+@pytest.mark.parametrize("D,bs,dt,gs", DISPATCH)
+def test_dequant_dispatch_paths(cuda, bits, meta, D, bs, dt, gs):
+    run_quant_case(cuda, 2, 2, D, bs, 48, dt, bits, gs, meta, [1, bs - 1 if bs > 1 else 1, 3 * bs + 5, 70],
+                   new_tokens=2, seed=15 + D + bs)
