@@ -65,6 +65,7 @@ class Workload:
     group: int = 64
     meta: int = F16
     outliers: float = 0.0
+    attn_g: int = 0  # > 0: decode attention with this many query heads per KV head instead of the gather
 
     # bytes of one token's rows of the local heads
     def in_row(self, h):
@@ -78,6 +79,8 @@ class Workload:
 
     @property
     def kernel(self):
+        if self.attn_g:
+            return "paged_decode_attn_kernel"
         return "gather_dequant_r1_kernel" if self.bits else "gather_rows_kernel"
 
     @property
@@ -102,6 +105,11 @@ WORKLOADS = {
         "scale/zero, batch 128, ctx U[1024,8192], 1% outliers x8; quantise-on-append 1 token/seq/layer, then "
         "dequantise-on-gather (bf16) of every layer", seed=0x5EED + 3, batch=128, ctx_lo=1024, ctx_hi=8192, bits=4,
         outliers=0.01),
+    "attn": Workload(
+        "attn", "KV append + paged decode attention HBM GB/s (decode step, Llama-3.1-8B shape)",
+        "decode step with attention reading the pool in place: 32 layers x 8 KV heads x 128, block 16, bf16, "
+        "32 query heads (4 per KV head), batch 64, ctx U[512,4096]; append 1 token/seq/layer, then paged decode "
+        "attention of every layer (no gathered copy)", seed=0x5EED + 2, attn_g=4),
 }
 
 
@@ -409,7 +417,9 @@ def run_llama70b(args, rank, world):
             moved = (nmov + n_in) * bb
             mig = {"blocks_per_rank": nmov, "bytes_per_rank": moved, "ms": round(mig_ms, 3),
                    "gbs_per_rank": round(moved / (mig_ms * 1e-3) / 1e9, 1),
-                   "what": "pack + ncclSend/ncclRecv (both directions) + unpack, rank pairs (r, r^1)"}
+                   "gbs_per_direction": round(nmov * bb / (mig_ms * 1e-3) / 1e9, 1),
+                   "what": "pack + ncclSend/ncclRecv + unpack, rank pairs (r, r^1) exchanging at once; "
+                           "bytes_per_rank counts sent + received, gbs_per_direction the sent bytes alone"}
         comm.close()
     if rank == 0:
         peak, kind = measured_peak()
@@ -504,6 +514,11 @@ def step_bytes(w, lens, heads, layers=None):
     i, s, m = w.in_row(heads), w.stored_row(heads), w.meta_row(heads)
     append = 2 * w.batch * layers * (i + s + m)
     blocks = int(((lens + w.block - 1) // w.block).sum())
+    if w.attn_g:
+        # attention reads every stored row once (no gathered copy written),
+        # plus the queries it reads and the outputs it writes
+        qo = 2 * w.batch * w.attn_g * i
+        return append, 2 * int(lens.sum()) * (s + m) + 4 * blocks + 4 * w.batch + qo
     gather_one = 2 * int(lens.sum()) * (s + m + i) + 4 * blocks + 4 * w.batch
     return append, gather_one
 
@@ -616,6 +631,10 @@ def run_reference(args, w, rank, world):
     """--impl reference: the reference's CPU path (the oracle port; the Rust
     reference cannot be built in this image) on all host cores."""
     if rank != 0:
+        return
+    if w.attn_g:
+        print(json.dumps({"impl": "reference", "unavailable": "the reference has no attention of its own on this "
+                          "path (it runs inside the external rmlx-nn Metal layer cache)"}))
         return
     threads = os.cpu_count() or 1
     steps, warm = max(args.steps // 5, 2), min(args.warmup, 2)
@@ -759,8 +778,18 @@ def main():
     slots_d = torch.from_numpy(slots).cuda()
     lens_steps = np.stack([(lens0 + s + 1).astype(np.int32) for s in range(W + K)])
     lens_d = torch.from_numpy(lens_steps).cuda()
-    out_k = torch.empty(int(lens_steps[-1].sum()) * H * D, device="cuda", dtype=torch.bfloat16)
-    out_v = torch.empty_like(out_k)
+    G = w.attn_g
+    if G:
+        # per-layer queries of the step, attention output, split workspace
+        q_d = rand_rows((L, B, H * G, D))
+        att_out = torch.empty((B, H * G, D), device="cuda", dtype=torch.bfloat16)
+        ws_bytes = pool.attention_workspace_size(G, B, int(lens_steps[-1].sum()))
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+        scale = 1.0 / float(np.sqrt(D))
+        out_k = out_v = None
+    else:
+        out_k = torch.empty(int(lens_steps[-1].sum()) * H * D, device="cuda", dtype=torch.bfloat16)
+        out_v = torch.empty_like(out_k)
     ls = B * H * D
 
     def launch_step(s, ev_pair=None):
@@ -773,8 +802,13 @@ def main():
         if ev_pair is not None:
             ev_pair[0].record(stream)
         for layer in range(L):
-            rc |= lib.rmlx_kv_gather(h, layer, bt_d.data_ptr(), bt.shape[1], lens_d[s].data_ptr(), B,
-                                     out_k.data_ptr(), out_v.data_ptr(), sp)
+            if G:
+                rc |= lib.rmlx_kv_decode_attention(h, layer, q_d[layer].data_ptr(), G, bt_d.data_ptr(), bt.shape[1],
+                                                   lens_d[s].data_ptr(), B, scale, att_out.data_ptr(),
+                                                   ws.data_ptr(), ws_bytes, sp)
+            else:
+                rc |= lib.rmlx_kv_gather(h, layer, bt_d.data_ptr(), bt.shape[1], lens_d[s].data_ptr(), B,
+                                         out_k.data_ptr(), out_v.data_ptr(), sp)
         if ev_pair is not None:
             ev_pair[1].record(stream)
         return rc
@@ -865,6 +899,11 @@ def main():
     d_lens = torch.empty(B, dtype=torch.int32, device="cuda")
     d_bt = torch.empty_like(bt_d)
     h2d = 2 * dk.numel() * 2 + 2 * B * 4 + host_bt.nbytes
+    if G:
+        # the step's queries for every layer come from the host too
+        pin_q = q_d.cpu().pin_memory()
+        dq = torch.empty_like(q_d)
+        h2d += q_d.numel() * 2
     barrier()
     torch.cuda.synchronize()
     t0 = time.perf_counter()
@@ -883,9 +922,16 @@ def main():
         d_lens.copy_(pin_lens, non_blocking=True)
         d_bt.copy_(pin_bt, non_blocking=True)
         rc |= lib.rmlx_kv_append(h, 0, L, dk.data_ptr(), dv.data_ptr(), ls, ts, hs, d_slots.data_ptr(), B, sp)
+        if G:
+            dq.copy_(pin_q, non_blocking=True)
         for layer in range(L):
-            rc |= lib.rmlx_kv_gather(h, layer, d_bt.data_ptr(), bt.shape[1], d_lens.data_ptr(), B,
-                                     out_k.data_ptr(), out_v.data_ptr(), sp)
+            if G:
+                rc |= lib.rmlx_kv_decode_attention(h, layer, dq[layer].data_ptr(), G, d_bt.data_ptr(), bt.shape[1],
+                                                   d_lens.data_ptr(), B, scale, att_out.data_ptr(), ws.data_ptr(),
+                                                   ws_bytes, sp)
+            else:
+                rc |= lib.rmlx_kv_gather(h, layer, d_bt.data_ptr(), bt.shape[1], d_lens.data_ptr(), B,
+                                         out_k.data_ptr(), out_v.data_ptr(), sp)
         if rc or pool.check():  # the step's status word, read back to the host
             raise SystemExit("launch or device-side validation error in the e2e loop")
     torch.cuda.synchronize()
@@ -899,7 +945,7 @@ def main():
     traffic = profile_traffic(w.profile, g_bytes)
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and not G:
         threads = os.cpu_count() or 1
         steps = 8 if not w.bits else 3
         gbs, _ = cpu_sample(w, steps, 1, threads, lens0, bt, slots, num_blocks)
@@ -918,7 +964,7 @@ def main():
                          "algorithmic_bytes_per_launch": int(g_bytes), "launch_ms": round(g_ms, 4)},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": 4, "ms_per_step": round(e2e_s / K * 1e3, 4)},
-            "gpu_launches": K * (1 + L),
+            "gpu_launches": K * (1 + (2 if G else 1) * L),
             "cpu_baseline": cpu,
             "clocks": clk,
         }), flush=True)

@@ -299,8 +299,8 @@ RMLX_API rmlx_status rmlx_kv_pool_layout(const rmlx_kv_pool* p, rmlx_pool_layout
 RMLX_API rmlx_status rmlx_kv_pool_check(rmlx_kv_pool* p, int32_t* device_error);
 
 /* Synchronous copies between host memory and pool bytes
- * [offset, offset + nbytes) (e.g. to save or restore blocks, the role of
- * save_prompt_cache / load_prompt_cache, prompt_cache.rs:63-210). */
+ * [offset, offset + nbytes) (raw byte images of the pool; the prompt-cache
+ * file format is rmlx_prompt_cache_save / _load below). */
 RMLX_API rmlx_status rmlx_kv_pool_read(rmlx_kv_pool* p, size_t offset, size_t nbytes, void* host_dst);
 RMLX_API rmlx_status rmlx_kv_pool_write(rmlx_kv_pool* p, size_t offset, size_t nbytes, const void* host_src);
 
@@ -329,6 +329,68 @@ RMLX_API rmlx_status rmlx_kv_append(rmlx_kv_pool* p, int32_t layer_begin, int32_
 #define RMLX_MAX_SEQS_PER_LAUNCH 8192
 RMLX_API rmlx_status rmlx_kv_gather(rmlx_kv_pool* p, int32_t layer, const int32_t* block_tables, int32_t block_table_stride,
                            const int32_t* seq_lens, int32_t num_seqs, void* out_k, void* out_v, void* stream);
+
+/* Paged decode attention: the consumer of the K/V tiles, reading them in
+ * place (no counterpart in the reference crate, whose attention runs inside
+ * the external rmlx-nn layer cache, kv_cache.rs:30,50; listed as the next
+ * step after the gather).  For sequence s and query head j of this pool's
+ * num_kv_heads x q_heads_per_kv heads (query head j reads KV head
+ * j / q_heads_per_kv):
+ *   out[s][j][:] = softmax(softmax_scale * q[s][j] . K[s]^T) V[s]
+ * over the seq_lens[s] rows that rmlx_kv_gather would return for (s, layer).
+ * q and out are [num_seqs][num_kv_heads * q_heads_per_kv][head_dim] in the
+ * pool's type; f32 scores and sums; a sequence of length 0 gives zeros.
+ * F16/BF16 pools with head_dim 64 or 128, q_heads_per_kv in [1, 16].
+ * workspace: at least rmlx_kv_attention_workspace_size(...) bytes for a
+ * launch whose seq_lens sum to at most max_total_tokens; a launch that needs
+ * more is flagged in the pool's device error word (rmlx_kv_pool_check bit 4)
+ * and leaves out unwritten. */
+RMLX_API rmlx_status rmlx_kv_attention_workspace_size(const rmlx_kv_pool* p, int32_t q_heads_per_kv, int32_t num_seqs,
+                                                      int64_t max_total_tokens, size_t* bytes);
+RMLX_API rmlx_status rmlx_kv_decode_attention(rmlx_kv_pool* p, int32_t layer, const void* q, int32_t q_heads_per_kv,
+                                              const int32_t* block_tables, int32_t block_table_stride,
+                                              const int32_t* seq_lens, int32_t num_seqs, float softmax_scale, void* out,
+                                              void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- Prompt cache files (prompt_cache.rs:63-210) --------------------------
+ * A sequence's K/V as a safetensors file: one [seq_len, head_dim] tensor per
+ * (layer, head) named layer_{l}_head_{h}_keys / layer_{l}_head_{h}_values
+ * (save_prompt_cache, :55-58), dtype F32/F16/BF16, optional string metadata
+ * under "__metadata__", serialised as the safetensors crate does (8-byte LE
+ * header length, compact JSON header, tensors ordered by name, header padded
+ * to 8 bytes with spaces).  A sequence of length 0 writes no tensors (:79).
+ * Heads are named by global index (cfg.head_offset + h).
+ *
+ * rmlx_prompt_cache_write / _read: host arrays [layers][heads][seq_len]
+ * [head_dim] of keys and of values <-> file.  _read takes the heads
+ * [head_offset, head_offset + num_kv_heads) of every layer the file holds
+ * (the file may hold other heads too) and fails if any is missing; cap_bytes
+ * is the size of each of keys and values.
+ * rmlx_prompt_cache_info: the file's layers and heads (largest index + 1, as
+ * load_prompt_cache derives them, :151-167), seq_len, head_dim, dtype (-1
+ * when the file holds no tensor) and its metadata as a JSON object ("" when
+ * absent; NUL-terminated, truncated to metadata_cap - 1 bytes).
+ * rmlx_prompt_cache_save: the sequence whose rows live in block_ids (host
+ * array, block table order) of every layer of the pool -> file (a quantised
+ * pool saves its dequantised rows).  rmlx_prompt_cache_load: file -> the
+ * rows of the caller-allocated blocks block_ids (ceil(seq_len / block_size)
+ * of them; rmlx_prompt_cache_info gives seq_len), through the pool's append;
+ * *seq_len = rows loaded.  Both synchronise `stream`. */
+RMLX_API rmlx_status rmlx_prompt_cache_write(const char* path, int32_t num_layers, int32_t num_kv_heads, int32_t head_offset,
+                                             int32_t seq_len, int32_t head_dim, int32_t dtype, const void* keys,
+                                             const void* values, const char* const* meta_keys,
+                                             const char* const* meta_values, int32_t num_meta);
+RMLX_API rmlx_status rmlx_prompt_cache_read(const char* path, int32_t num_layers, int32_t num_kv_heads, int32_t head_offset,
+                                            int32_t head_dim, int32_t dtype, void* keys, void* values, size_t cap_bytes,
+                                            int32_t* seq_len);
+RMLX_API rmlx_status rmlx_prompt_cache_info(const char* path, int32_t* num_layers, int32_t* num_kv_heads, int32_t* seq_len,
+                                            int32_t* head_dim, int32_t* dtype, char* metadata_json, size_t metadata_cap,
+                                            size_t* metadata_len);
+RMLX_API rmlx_status rmlx_prompt_cache_save(rmlx_kv_pool* p, const int32_t* block_ids, int32_t num_block_ids, int32_t seq_len,
+                                            const char* path, const char* const* meta_keys,
+                                            const char* const* meta_values, int32_t num_meta, void* stream);
+RMLX_API rmlx_status rmlx_prompt_cache_load(rmlx_kv_pool* p, const char* path, const int32_t* block_ids, int32_t num_block_ids,
+                                            int32_t* seq_len, void* stream);
 
 /* Block copy for copy-on-write / fork: every tile of block src[i] is copied
  * to block dst[i] (all layers, K and V, all heads of the pool).  src/dst are

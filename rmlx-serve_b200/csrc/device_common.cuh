@@ -16,6 +16,7 @@ namespace rmlx {
 enum : int32_t {
   DEV_ERR_SLOT = 1,   // slot_mapping entry >= num_blocks * block_size
   DEV_ERR_BLOCK = 2,  // block-table / copy id outside [0, num_blocks)
+  DEV_ERR_WORKSPACE = 4,  // a launch's splits exceed the workspace it was given
 };
 
 // 16-byte streaming load through the non-coherent path without L1

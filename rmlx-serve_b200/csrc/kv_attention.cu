@@ -1,0 +1,433 @@
+// Paged decode attention over the pool: the consumer of the K/V tiles, reading
+// them in place instead of through a gathered copy.
+//
+// For each sequence s and query head j (grouped: q heads g*G .. g*G+G-1 share
+// KV head g of this pool), out = softmax(scale * q K^T) V over the sequence's
+// len tokens, K/V rows located through the block table exactly like the
+// gather (token t: block bt[s][t / block_size], row t % block_size).
+//
+// Split over the sequence (flash-decoding): a work item is (split of 256
+// tokens, KV head), one warp per item.  A warp streams its split in chunks of
+// 16 tokens through shared memory (cp.async, three stages per warp) and runs
+// both products on the tensor cores with mma.sync m16n8k16 (f16/bf16 inputs,
+// f32 accumulation): S = Q K^T with the G query heads as the M rows, then
+// O += P V with P (the exponentiated scores, rounded to the pool's type) as
+// the A operand.  An online softmax in the log2 domain keeps a running max
+// and sum per query head.  Each item writes its unnormalised O, max and sum
+// to a workspace; a second kernel combines the splits of each (sequence,
+// query head) and writes the output in the pool's type.
+//
+// The kernel is HBM-bound: per token and KV head it reads 2 x head_dim x 2
+// bytes and does 4 x G x head_dim flops (G = 4..8: 8..16 flops per byte),
+// two orders of magnitude under the tensor cores' ridge point, so the legacy
+// warp-level mma is not the limit; what matters is that every K/V byte is
+// read once with enough bytes in flight.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+
+#include "kv_pool_internal.cuh"
+
+namespace rmlx {
+
+constexpr int ATT_SPLIT = 256;  // tokens per work item
+constexpr int ATT_CHUNK = 16;   // tokens per tensor-core step
+constexpr int ATT_STAGES = 3;   // chunks in flight per warp
+constexpr int ATT_WARPS = 4;    // warps per CTA (independent items)
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <int DT>
+__device__ __forceinline__ void mma16816(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  if (DT == RMLX_BF16) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  } else {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr)
+               : "memory");
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr)
+               : "memory");
+}
+// 16-byte async copy; src_bytes = 0 fills the destination with zeros and reads nothing.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+template <int DT>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  if (DT == RMLX_BF16) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  } else {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+}
+
+// Shared-memory layout of one stage: K rows then V rows of a 16-token chunk,
+// row-major, 16-byte column chunk c of row r stored at slot c ^ (r & 7) so
+// that the 8 row addresses of every ldmatrix hit 8 different bank groups.
+template <int DT, int HD>
+__global__ void __launch_bounds__(ATT_WARPS * 32, 2)
+    paged_decode_attn_kernel(PoolGeo g, int layer, const uint8_t* __restrict__ q, int G,
+                             const int32_t* __restrict__ bt, int bt_stride, const int32_t* __restrict__ lens,
+                             int nseq, float scale_log2, float* __restrict__ part_o, float* __restrict__ part_ml,
+                             int64_t cap_splits, int32_t* err) {
+  constexpr int ROWB = HD * 2;  // bytes of one K or V row
+  constexpr int CPR = ROWB / 16;
+  constexpr int KT = HD / 16;  // k-steps of S = Q K^T
+  constexpr int NT = HD / 8;   // n-tiles of O
+  constexpr int STAGE = 2 * ATT_CHUNK * ROWB;
+  constexpr unsigned FULL = 0xffffffffu;
+  extern __shared__ __align__(128) uint8_t smem[];
+  int32_t* cub = reinterpret_cast<int32_t*>(smem);
+  int32_t* cut = cub + nseq + 1;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const size_t scan_bytes = ((size_t)2 * (nseq + 1) * 4 + 127) & ~(size_t)127;
+  const uint32_t wbuf = (uint32_t)__cvta_generic_to_shared(smem + scan_bytes) + warp * ATT_STAGES * STAGE;
+  pdl_wait();
+  pdl_release();
+  scan_seq_lens(lens, nseq, ATT_SPLIT, cub, cut);
+  const int64_t nsplit = cub[nseq];
+  if (nsplit > cap_splits) {
+    if (threadIdx.x == 0) atomicOr(err, DEV_ERR_WORKSPACE);
+    return;
+  }
+  const int64_t items = nsplit * g.heads;
+  const int qheads = g.heads * G;
+  const int r = lane >> 2, c = lane & 3;
+  const int64_t vdelta = (int64_t)g.heads * g.tile_bytes;  // V tile of (block, layer, head) after its K tile
+  const bool aligned_blocks = (g.bs % ATT_CHUNK) == 0;     // a chunk never crosses a block
+  const int64_t nwarps = (int64_t)gridDim.x * ATT_WARPS;
+
+  for (int64_t it = (int64_t)blockIdx.x * ATT_WARPS + warp; it < items; it += nwarps) {
+    const int h = (int)(it % g.heads);
+    const int64_t sg = it / g.heads;
+    const int s = find_seq(cub, nseq, sg);
+    const int t_begin = (int)(sg - cub[s]) * ATT_SPLIT;
+    const int t_end = min(cut[s + 1] - cut[s], t_begin + ATT_SPLIT);
+    const int nchunks = (t_end - t_begin + ATT_CHUNK - 1) / ATT_CHUNK;
+    const int32_t* btrow = bt + (int64_t)s * bt_stride;
+
+    // Q as A fragments (rows = query heads, zero beyond G).
+    uint32_t qa[KT][4];
+    const uint8_t* qbase = q + ((int64_t)s * qheads + (int64_t)h * G) * ROWB;
+#pragma unroll
+    for (int kk = 0; kk < KT; ++kk)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int row = r + (i & 1) * 8, col = kk * 16 + 2 * c + (i >> 1) * 8;
+        qa[kk][i] = row < G ? __ldg(reinterpret_cast<const uint32_t*>(qbase + (int64_t)row * ROWB + col * 2)) : 0u;
+      }
+
+    auto load_chunk = [&](int ci) {
+      const uint32_t dst = wbuf + (ci % ATT_STAGES) * STAGE;
+      const int tc = t_begin + ci * ATT_CHUNK;
+      if (aligned_blocks) {
+        // the chunk's 16 rows are contiguous in one K tile (and one V tile)
+        const int32_t blk = __ldg(btrow + tc / g.bs);
+        const bool ok = blk >= 0 && blk < g.nblocks;
+        if (!ok && lane == 0) atomicOr(err, DEV_ERR_BLOCK);
+        const uint8_t* src = ok ? g.base + g.tile_off(blk, layer, 0, h) + (int64_t)(tc % g.bs) * ROWB : g.base;
+#pragma unroll
+        for (int i = 0; i < (ATT_CHUNK * CPR) / 32; ++i) {
+          const int idx = lane + 32 * i, row = idx / CPR, ch = idx % CPR;
+          const int n = (ok && tc + row < t_end) ? 16 : 0;
+          const uint32_t so = row * ROWB + ((ch ^ (row & 7)) << 4);
+          const uint8_t* p = n ? src + row * ROWB + ch * 16 : g.base;
+          cp_async16(dst + so, p, n);
+          cp_async16(dst + ATT_CHUNK * ROWB + so, n ? p + vdelta : g.base, n);
+        }
+      } else {
+        // lanes 0..15 locate row (lane & 15); the others take it by shuffle
+        const int t = tc + (lane & 15);
+        const uint8_t* src = g.base;
+        int nb = 0;
+        if (t < t_end) {
+          const int32_t blk = __ldg(btrow + t / g.bs);
+          if (blk >= 0 && blk < g.nblocks) {
+            src = g.base + g.tile_off(blk, layer, 0, h) + (int64_t)(t % g.bs) * ROWB;
+            nb = 16;
+          } else if (lane < 16) {
+            atomicOr(err, DEV_ERR_BLOCK);
+          }
+        }
+        const unsigned long long sp = reinterpret_cast<unsigned long long>(src);
+#pragma unroll
+        for (int i = 0; i < (ATT_CHUNK * CPR) / 32; ++i) {
+          const int idx = lane + 32 * i, row = idx / CPR, ch = idx % CPR;
+          const uint8_t* rp = reinterpret_cast<const uint8_t*>(__shfl_sync(FULL, sp, row));
+          const int n = __shfl_sync(FULL, nb, row);
+          const uint32_t so = row * ROWB + ((ch ^ (row & 7)) << 4);
+          cp_async16(dst + so, n ? rp + ch * 16 : g.base, n);
+          cp_async16(dst + ATT_CHUNK * ROWB + so, n ? rp + vdelta + ch * 16 : g.base, n);
+        }
+      }
+      cp_async_commit();
+    };
+
+    float o[NT][4];
+#pragma unroll
+    for (int d = 0; d < NT; ++d) o[d][0] = o[d][1] = o[d][2] = o[d][3] = 0.0f;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;  // rows r and r + 8
+
+#pragma unroll
+    for (int ci = 0; ci < ATT_STAGES - 1; ++ci) {
+      if (ci < nchunks) load_chunk(ci);
+      else cp_async_commit();  // keep one group per slot so the wait count stays fixed
+    }
+    for (int ci = 0; ci < nchunks; ++ci) {
+      if (ci + ATT_STAGES - 1 < nchunks) load_chunk(ci + ATT_STAGES - 1);
+      else cp_async_commit();
+      cp_async_wait<ATT_STAGES - 1>();
+      __syncwarp();
+      const uint32_t kb = wbuf + (ci % ATT_STAGES) * STAGE, vb = kb + ATT_CHUNK * ROWB;
+      const int tc = t_begin + ci * ATT_CHUNK;
+
+      // S = Q K^T: two n-tiles of 8 tokens
+      float sacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+      for (int kk = 0; kk < KT; ++kk) {
+        const int mi = lane >> 3, row = ((mi >> 1) << 3) + (lane & 7), ch = 2 * kk + (mi & 1);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(kb + row * ROWB + ((ch ^ (row & 7)) << 4), b0, b1, b2, b3);
+        mma16816<DT>(sacc[0], qa[kk], b0, b1);
+        mma16816<DT>(sacc[1], qa[kk], b2, b3);
+      }
+      // online softmax (log2 domain), masking tokens past the split's end
+      float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const bool valid = tc + 8 * j + 2 * c + e < t_end;
+          sacc[j][e] = valid ? sacc[j][e] * scale_log2 : -INFINITY;
+          sacc[j][2 + e] = valid ? sacc[j][2 + e] * scale_log2 : -INFINITY;
+          mx0 = fmaxf(mx0, sacc[j][e]);
+          mx1 = fmaxf(mx1, sacc[j][2 + e]);
+        }
+      mx0 = fmaxf(mx0, __shfl_xor_sync(FULL, mx0, 1));
+      mx0 = fmaxf(mx0, __shfl_xor_sync(FULL, mx0, 2));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(FULL, mx1, 1));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(FULL, mx1, 2));
+      const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);  // finite: every chunk has a valid token
+      const float a0 = ex2(m0 - n0), a1 = ex2(m1 - n1);
+      m0 = n0;
+      m1 = n1;
+      float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          sacc[j][e] = ex2(sacc[j][e] - n0);
+          sacc[j][2 + e] = ex2(sacc[j][2 + e] - n1);
+          ps0 += sacc[j][e];
+          ps1 += sacc[j][2 + e];
+        }
+      l0 = l0 * a0 + ps0;
+      l1 = l1 * a1 + ps1;
+      if (__any_sync(FULL, a0 != 1.0f || a1 != 1.0f)) {
+#pragma unroll
+        for (int d = 0; d < NT; ++d) {
+          o[d][0] *= a0;
+          o[d][1] *= a0;
+          o[d][2] *= a1;
+          o[d][3] *= a1;
+        }
+      }
+      // O += P V; P's accumulator layout is the A-fragment layout
+      uint32_t pa[4];
+      pa[0] = pack2<DT>(sacc[0][0], sacc[0][1]);
+      pa[1] = pack2<DT>(sacc[0][2], sacc[0][3]);
+      pa[2] = pack2<DT>(sacc[1][0], sacc[1][1]);
+      pa[3] = pack2<DT>(sacc[1][2], sacc[1][3]);
+#pragma unroll
+      for (int d2 = 0; d2 < HD / 16; ++d2) {
+        const int mi = lane >> 3, row = ((mi & 1) << 3) + (lane & 7), ch = 2 * d2 + (mi >> 1);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(vb + row * ROWB + ((ch ^ (row & 7)) << 4), b0, b1, b2, b3);
+        mma16816<DT>(o[2 * d2], pa, b0, b1);
+        mma16816<DT>(o[2 * d2 + 1], pa, b2, b3);
+      }
+      __syncwarp();  // the stage is overwritten by the next load
+    }
+    cp_async_wait<0>();
+    __syncwarp();
+
+    l0 += __shfl_xor_sync(FULL, l0, 1);
+    l0 += __shfl_xor_sync(FULL, l0, 2);
+    l1 += __shfl_xor_sync(FULL, l1, 1);
+    l1 += __shfl_xor_sync(FULL, l1, 2);
+    float* po = part_o + it * (int64_t)G * HD;
+    float* pml = part_ml + it * (int64_t)2 * G;
+#pragma unroll
+    for (int d = 0; d < NT; ++d) {
+      if (r < G) *reinterpret_cast<float2*>(po + r * HD + 8 * d + 2 * c) = make_float2(o[d][0], o[d][1]);
+      if (r + 8 < G) *reinterpret_cast<float2*>(po + (r + 8) * HD + 8 * d + 2 * c) = make_float2(o[d][2], o[d][3]);
+    }
+    if (c == 0) {
+      if (r < G) *reinterpret_cast<float2*>(pml + 2 * r) = make_float2(m0, l0);
+      if (r + 8 < G) *reinterpret_cast<float2*>(pml + 2 * (r + 8)) = make_float2(m1, l1);
+    }
+  }
+}
+
+// One warp per (sequence, query head): combine the splits' (O, max, sum) and
+// write out[s][qh][:] in the pool's type.  A sequence of length 0 gets zeros.
+template <int DT, int HD>
+__global__ void __launch_bounds__(256) attn_combine_kernel(const int32_t* __restrict__ lens, int nseq, int heads, int G,
+                                                           const float* __restrict__ part_o,
+                                                           const float* __restrict__ part_ml, uint8_t* __restrict__ out,
+                                                           int64_t cap_splits) {
+  constexpr int EPL = HD / 32;  // elements per lane
+  extern __shared__ int32_t cs[];
+  int32_t* cub = cs;
+  int32_t* cut = cs + nseq + 1;
+  pdl_wait();
+  pdl_release();
+  scan_seq_lens(lens, nseq, ATT_SPLIT, cub, cut);
+  if (cub[nseq] > cap_splits) return;  // flagged by the split kernel
+  const int lane = threadIdx.x & 31;
+  const int qheads = heads * G;
+  const int64_t total = (int64_t)nseq * qheads;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; w < total; w += nwarps) {
+    const int s = (int)(w / qheads), qh = (int)(w % qheads), h = qh / G, j = qh % G;
+    const int n = cub[s + 1] - cub[s];
+    float mx = -INFINITY;
+    for (int i = 0; i < n; ++i) mx = fmaxf(mx, __ldg(part_ml + ((int64_t)(cub[s] + i) * heads + h) * 2 * G + 2 * j));
+    float acc[EPL];
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) acc[e] = 0.0f;
+    float L = 0.0f;
+    for (int i = 0; i < n; ++i) {
+      const int64_t item = (int64_t)(cub[s] + i) * heads + h;
+      const float2 ml = __ldg(reinterpret_cast<const float2*>(part_ml + item * 2 * G) + j);
+      const float wgt = ex2(ml.x - mx);
+      L += ml.y * wgt;
+      const float* po = part_o + (item * G + j) * HD + lane * EPL;
+#pragma unroll
+      for (int e = 0; e < EPL; e += 2) {
+        const float2 v = __ldg(reinterpret_cast<const float2*>(po + e));
+        acc[e] += wgt * v.x;
+        acc[e + 1] += wgt * v.y;
+      }
+    }
+    const float inv = n ? 1.0f / L : 0.0f;
+    uint32_t wv[EPL / 2];
+#pragma unroll
+    for (int e = 0; e < EPL; e += 2) wv[e / 2] = pack2<DT>(acc[e] * inv, acc[e + 1] * inv);
+    uint8_t* dst = out + ((int64_t)s * qheads + qh) * HD * 2 + lane * EPL * 2;
+    if (EPL == 4) *reinterpret_cast<uint2*>(dst) = make_uint2(wv[0], wv[1]);
+    else *reinterpret_cast<uint32_t*>(dst) = wv[0];
+  }
+}
+
+}  // namespace rmlx
+
+using namespace rmlx;
+
+namespace {
+
+// Bytes of workspace per split and KV head: G x head_dim partial outputs and
+// a (max, sum) pair per query head, all f32.
+size_t split_bytes(int heads, int G, int hd) { return (size_t)heads * G * (hd + 2) * sizeof(float); }
+
+using AttnFn = void (*)(PoolGeo, int, const uint8_t*, int, const int32_t*, int, const int32_t*, int, float, float*,
+                        float*, int64_t, int32_t*);
+using CombineFn = void (*)(const int32_t*, int, int, int, const float*, const float*, uint8_t*, int64_t);
+
+}  // namespace
+
+extern "C" {
+
+rmlx_status rmlx_kv_attention_workspace_size(const rmlx_kv_pool* p, int32_t q_heads_per_kv, int32_t num_seqs,
+                                             int64_t max_total_tokens, size_t* bytes) {
+  if (!p || !bytes) return fail(RMLX_E_BAD_ARG, "NULL pool or bytes");
+  if (q_heads_per_kv < 1 || q_heads_per_kv > 16) return fail(RMLX_E_BAD_ARG, "q_heads_per_kv must be in [1, 16]");
+  if (num_seqs < 0 || max_total_tokens < 0) return fail(RMLX_E_BAD_ARG, "negative num_seqs or max_total_tokens");
+  const int64_t splits = max_total_tokens / ATT_SPLIT + num_seqs;
+  *bytes = (size_t)splits * split_bytes(p->cfg.num_kv_heads, q_heads_per_kv, p->cfg.head_dim);
+  return RMLX_OK;
+}
+
+rmlx_status rmlx_kv_decode_attention(rmlx_kv_pool* p, int32_t layer, const void* q, int32_t q_heads_per_kv,
+                                     const int32_t* block_tables, int32_t block_table_stride, const int32_t* seq_lens,
+                                     int32_t num_seqs, float softmax_scale, void* out, void* workspace,
+                                     size_t workspace_bytes, void* stream) {
+  if (!p) return fail(RMLX_E_BAD_ARG, "NULL pool");
+  const rmlx_pool_config& c = p->cfg;
+  if (c.quant_bits != 0) return fail(RMLX_E_BAD_ARG, "decode attention reads f16/bf16 pools, not quantised ones");
+  if (c.dtype != RMLX_F16 && c.dtype != RMLX_BF16) return fail(RMLX_E_BAD_ARG, "decode attention needs an F16 or BF16 pool");
+  if (c.head_dim != 64 && c.head_dim != 128) return fail(RMLX_E_BAD_ARG, "decode attention supports head_dim 64 or 128");
+  if (q_heads_per_kv < 1 || q_heads_per_kv > 16) return fail(RMLX_E_BAD_ARG, "q_heads_per_kv must be in [1, 16]");
+  if (layer < 0 || layer >= c.num_layers) return fail(RMLX_E_RANGE, "layer %d out of range", layer);
+  if (num_seqs < 0 || num_seqs > RMLX_MAX_SEQS_PER_LAUNCH) return fail(RMLX_E_BAD_ARG, "num_seqs out of range");
+  if (num_seqs == 0) return RMLX_OK;
+  if (!q || !out || !block_tables || !seq_lens || !workspace) return fail(RMLX_E_BAD_ARG, "NULL argument");
+  if (!aligned16(q) || !aligned16(out) || !aligned16(workspace))
+    return fail(RMLX_E_BAD_ARG, "q, out and workspace must be 16-byte aligned");
+  if (block_table_stride < 0) return fail(RMLX_E_BAD_ARG, "negative block_table_stride");
+  if (!(softmax_scale > 0.0f) || softmax_scale > 1e30f) return fail(RMLX_E_BAD_ARG, "softmax_scale must be positive");
+  const int G = q_heads_per_kv, hd = c.head_dim, heads = c.num_kv_heads;
+  const size_t per_split = split_bytes(heads, G, hd);
+  const int64_t cap = (int64_t)(workspace_bytes / per_split);
+  if (cap < 1) return fail(RMLX_E_BAD_ARG, "workspace smaller than one split");
+  // partial outputs, then the (max, sum) pairs; heads x G x head_dim is a
+  // multiple of 64 floats, so the second array starts 16-byte aligned
+  float* part_o = static_cast<float*>(workspace);
+  float* part_ml = part_o + (size_t)cap * heads * G * hd;
+  DeviceGuard dg(p->device);
+  cudaStream_t st = (cudaStream_t)stream;
+  const bool bf = c.dtype == RMLX_BF16;
+  AttnFn fa = hd == 128 ? (bf ? paged_decode_attn_kernel<RMLX_BF16, 128> : paged_decode_attn_kernel<RMLX_F16, 128>)
+                        : (bf ? paged_decode_attn_kernel<RMLX_BF16, 64> : paged_decode_attn_kernel<RMLX_F16, 64>);
+  CombineFn fc = hd == 128 ? (bf ? attn_combine_kernel<RMLX_BF16, 128> : attn_combine_kernel<RMLX_F16, 128>)
+                           : (bf ? attn_combine_kernel<RMLX_BF16, 64> : attn_combine_kernel<RMLX_F16, 64>);
+  const size_t scan_bytes = ((size_t)2 * (num_seqs + 1) * 4 + 127) & ~(size_t)127;
+  const size_t smem = scan_bytes + (size_t)ATT_WARPS * ATT_STAGES * 2 * ATT_CHUNK * hd * 2;
+  rmlx_status s;
+  if ((s = prepare_smem(fa, smem)) != RMLX_OK) return s;
+  const int grid = persistent_grid(fa, ATT_WARPS * 32, smem, p->num_sms);
+  const float scale_log2 = softmax_scale * 1.4426950408889634f;  // log2(e)
+  cudaError_t e = launch_pdl(fa, dim3(grid), dim3(ATT_WARPS * 32), smem, st, p->geo(), (int)layer,
+                             static_cast<const uint8_t*>(q), G, block_tables, (int)block_table_stride, seq_lens,
+                             (int)num_seqs, scale_log2, part_o, part_ml, cap, p->err);
+  if (e != cudaSuccess) return cuda_check(e, "decode attention launch");
+  const size_t csmem = (size_t)2 * (num_seqs + 1) * 4;
+  if ((s = prepare_smem(fc, csmem)) != RMLX_OK) return s;
+  const int64_t warps = (int64_t)num_seqs * heads * G;
+  const int cgrid = (int)std::min<int64_t>((warps + 7) / 8, (int64_t)p->num_sms * 8);
+  e = launch_pdl(fc, dim3(cgrid), dim3(256), csmem, st, seq_lens, (int)num_seqs, heads, G, part_o, part_ml,
+                 static_cast<uint8_t*>(out), cap);
+  if (e != cudaSuccess) return cuda_check(e, "attention combine launch");
+  return cuda_check(cudaGetLastError(), "decode attention launch");
+}
+
+}  // extern "C"

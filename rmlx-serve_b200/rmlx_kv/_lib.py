@@ -149,7 +149,19 @@ _sig("rmlx_kv_pool_write", st, vp, C.c_size_t, C.c_size_t, vp)
 _sig("rmlx_kv_append", st, vp, C.c_int32, C.c_int32, vp, vp, C.c_int64, C.c_int64, C.c_int64, vp,
      C.c_int32, vp)
 _sig("rmlx_kv_gather", st, vp, C.c_int32, vp, C.c_int32, vp, C.c_int32, vp, vp, vp)
+_sig("rmlx_kv_attention_workspace_size", st, vp, C.c_int32, C.c_int32, C.c_int64, C.POINTER(C.c_size_t))
+_sig("rmlx_kv_decode_attention", st, vp, C.c_int32, vp, C.c_int32, vp, C.c_int32, vp, C.c_int32, C.c_float, vp, vp,
+     C.c_size_t, vp)
 _sig("rmlx_kv_copy_blocks", st, vp, vp, vp, C.c_int32, vp)
+cpp = C.POINTER(C.c_char_p)
+_sig("rmlx_prompt_cache_write", st, C.c_char_p, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, vp,
+     vp, cpp, cpp, C.c_int32)
+_sig("rmlx_prompt_cache_read", st, C.c_char_p, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, vp, vp, C.c_size_t,
+     C.POINTER(C.c_int32))
+_sig("rmlx_prompt_cache_info", st, C.c_char_p, C.POINTER(C.c_int32), C.POINTER(C.c_int32), C.POINTER(C.c_int32),
+     C.POINTER(C.c_int32), C.POINTER(C.c_int32), C.c_char_p, C.c_size_t, C.POINTER(C.c_size_t))
+_sig("rmlx_prompt_cache_save", st, vp, i32p, C.c_int32, C.c_int32, C.c_char_p, cpp, cpp, C.c_int32, vp)
+_sig("rmlx_prompt_cache_load", st, vp, C.c_char_p, i32p, C.c_int32, C.POINTER(C.c_int32), vp)
 _sig("rmlx_kv_pack_blocks", st, vp, vp, C.c_int32, vp, vp)
 _sig("rmlx_kv_unpack_blocks", st, vp, vp, C.c_int32, vp, vp)
 _sig("rmlx_hash_block_chains", st, vp, vp, vp, C.c_int32, C.c_int32, vp, vp, vp)

@@ -80,6 +80,19 @@ class SequenceBlocks:
             self.lens[s] = pos + 1
         return np.array(src, dtype=np.int32), np.array(dst, dtype=np.int32), slots
 
+    def trim(self, seq: int, n: int) -> List[int]:
+        """Drop the last n tokens of `seq` (all of them when n >= its length,
+        as trim_prompt_cache, prompt_cache.rs:218-226); blocks that no longer
+        hold a token lose this sequence's reference.  Returns those blocks."""
+        keep = max(self.lens[seq] - int(n), 0)
+        nb = (keep + self.bs - 1) // self.bs
+        dropped = self.tables[seq][nb:]
+        for b in dropped:
+            self.mgr.free(b)
+        self.tables[seq] = self.tables[seq][:nb]
+        self.lens[seq] = keep
+        return dropped
+
     def block_table(self) -> np.ndarray:
         """[num_seqs, max blocks] int32, rows padded with 0."""
         width = max([len(t) for t in self.tables] + [1])

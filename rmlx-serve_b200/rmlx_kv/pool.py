@@ -113,6 +113,22 @@ class KVPool:
         check(lib.rmlx_kv_gather(self._h, layer, _ptr(block_tables), block_table_stride, _ptr(seq_lens),
                                  num_seqs, _ptr(out_k), _ptr(out_v), _stream(stream, self.device)))
 
+    def attention_workspace_size(self, q_heads_per_kv: int, num_seqs: int, max_total_tokens: int) -> int:
+        n = C.c_size_t()
+        check(lib.rmlx_kv_attention_workspace_size(self._h, q_heads_per_kv, num_seqs, max_total_tokens, C.byref(n)))
+        return n.value
+
+    def decode_attention(self, layer: int, q, q_heads_per_kv: int, block_tables, block_table_stride: int, seq_lens,
+                         num_seqs: int, softmax_scale: float, out, workspace, workspace_bytes: int = None,
+                         stream=None) -> None:
+        """out = softmax(scale * q K^T) V per (sequence, query head), reading
+        the pool's tiles through the block table (no gathered copy)."""
+        if workspace_bytes is None:
+            workspace_bytes = workspace.numel() * workspace.element_size()
+        check(lib.rmlx_kv_decode_attention(self._h, layer, _ptr(q), q_heads_per_kv, _ptr(block_tables),
+                                           block_table_stride, _ptr(seq_lens), num_seqs, softmax_scale, _ptr(out),
+                                           _ptr(workspace), workspace_bytes, _stream(stream, self.device)))
+
     def copy_blocks(self, src, dst, n: int, stream=None) -> None:
         check(lib.rmlx_kv_copy_blocks(self._h, _ptr(src), _ptr(dst), n, _stream(stream, self.device)))
 

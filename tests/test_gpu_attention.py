@@ -1,0 +1,175 @@
+"""GPU numerics of the paged decode attention against a float64 reference.
+
+The reference computes softmax(scale * q K^T) V in float64 from the K/V rows
+that the gather returns for the same block tables (the gather itself is
+bit-exact against the oracle in test_gpu_paged.py).  Tolerances, from the
+kernel's arithmetic: scores and sums in f32 from exact products of the
+16-bit inputs; the exponentiated scores P are rounded to the pool's type
+before P V (relative error 2^-9 for bf16, 2^-12 for f16 per weight), and the
+output is rounded to the pool's type.  With |V| <~ 4.5 that bounds the
+error by about 4 * 2^-9 * 4.5 = 0.035 (bf16) and 0.005 (f16); the tests use
+max-abs 0.03 / 0.004 and an RMS bound ten times tighter.
+"""
+import numpy as np
+import pytest
+
+import oracle as orc
+import rmlx_kv
+from helpers import block_tables, to_dev
+
+pytestmark = pytest.mark.gpu
+
+TOL = {orc.BF16: (0.03, 0.003), orc.F16: (0.004, 0.0004)}
+
+
+def _pool(L, H, D, bs, N, dt, seed):
+    pool = rmlx_kv.KVPool(L, H, D, bs, N, dtype=dt)
+    rng = np.random.default_rng(seed)
+    vals = rng.standard_normal(pool.layout.bytes // 2, dtype=np.float32)
+    pool.write(orc.f32_to_dtype(vals, dt).view(np.uint8))
+    return pool, rng
+
+
+def _reference(pool, layer, q, G, bt, lens, scale, dt, cuda):
+    """float64 attention over the gathered K/V: out [B, H*G, D]."""
+    import torch
+    H, D = pool.cfg.num_kv_heads, pool.cfg.head_dim
+    tot = int(lens.sum())
+    ok = torch.empty(max(tot * H * D, 8), dtype=torch.int16, device=cuda)
+    ov = torch.empty_like(ok)
+    pool.gather(layer, to_dev(bt), bt.shape[1], to_dev(lens.astype(np.int32)), len(lens), ok, ov)
+    torch.cuda.synchronize()
+    k = orc.dtype_to_f32(ok.cpu().numpy().view(np.uint16)[:tot * H * D], dt).astype(np.float64)
+    v = orc.dtype_to_f32(ov.cpu().numpy().view(np.uint16)[:tot * H * D], dt).astype(np.float64)
+    qf = orc.dtype_to_f32(q, dt).astype(np.float64).reshape(len(lens), H * G, D)
+    out = np.zeros_like(qf)
+    o = 0
+    for s, n in enumerate(lens):
+        n = int(n)
+        ks = k[o * H * D:(o + n) * H * D].reshape(H, n, D)
+        vs = v[o * H * D:(o + n) * H * D].reshape(H, n, D)
+        o += n
+        if n == 0:
+            continue
+        for j in range(H * G):
+            sc = ks[j // G] @ qf[s, j] * scale
+            p = np.exp(sc - sc.max())
+            out[s, j] = (p / p.sum()) @ vs[j // G]
+    return out
+
+
+def run_attn(cuda, L, H, D, bs, N, dt, G, lens, seed, layer=0, extra_tokens=0):
+    import torch
+    pool, rng = _pool(L, H, D, bs, N, dt, seed)
+    lens = np.array(lens, dtype=np.int64)
+    bt, _ = block_tables(rng, lens, bs, N)
+    q = orc.f32_to_dtype(rng.standard_normal((len(lens), H * G, D), dtype=np.float32), dt)
+    scale = 1.0 / np.sqrt(D)
+    ws_bytes = pool.attention_workspace_size(G, len(lens), int(lens.sum()) + extra_tokens)
+    ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=cuda)
+    out = torch.full((len(lens), H * G, D), -7, dtype=torch.int16, device=cuda)
+    pool.decode_attention(layer, to_dev(q), G, to_dev(bt), bt.shape[1], to_dev(lens.astype(np.int32)), len(lens),
+                          scale, out, ws)
+    torch.cuda.synchronize()
+    assert pool.check() == 0
+    got = orc.dtype_to_f32(out.cpu().numpy().view(np.uint16), dt).astype(np.float64)
+    want = _reference(pool, layer, q, G, bt, lens, scale, dt, cuda)
+    err = np.abs(got - want)
+    mx, rms = TOL[dt]
+    assert np.isfinite(got).all()
+    assert err.max() <= mx, f"max abs error {err.max()}"
+    assert np.sqrt((err ** 2).mean()) <= rms, f"rms error {np.sqrt((err ** 2).mean())}"
+    zero = lens == 0
+    assert (got[zero] == 0).all()
+    pool.close()
+    return err
+
+
+@pytest.mark.parametrize("dt", [orc.BF16, orc.F16])
+def test_config1_shape(cuda, dt):
+    """8 KV heads x 128, block 16, 4 query heads per KV head, prompts 37/128/255/512 (+1)."""
+    run_attn(cuda, 1, 8, 128, 16, 256, dt, 4, [38, 129, 256, 513], seed=60)
+
+
+@pytest.mark.parametrize("G", [1, 8, 16])
+def test_group_sizes(cuda, G):
+    run_attn(cuda, 2, 2, 128, 16, 128, orc.BF16, G, [1, 17, 300, 700], seed=61 + G, layer=1)
+
+
+@pytest.mark.parametrize("bs", [1, 8, 32, 48])
+def test_block_sizes(cuda, bs):
+    """bs 1 and 8: a 16-token chunk spans several blocks (row-by-row copies);
+    32 and 48: several chunks per block."""
+    N = 600 // bs + 80
+    run_attn(cuda, 1, 2, 128, bs, N, orc.BF16, 4, [3, 16, 31, 257], seed=62 + bs)
+
+
+@pytest.mark.parametrize("dt", [orc.BF16, orc.F16])
+def test_head_dim_64_and_ragged(cuda, dt):
+    run_attn(cuda, 1, 4, 64, 16, 256, dt, 2, [0, 1, 15, 16, 17, 255, 256, 257, 1000], seed=63)
+
+
+def test_long_sequences_many_splits(cuda):
+    """8192 and 5000 tokens: 32 and 20 splits combined per query head."""
+    run_attn(cuda, 1, 1, 128, 16, 900, orc.BF16, 8, [8192, 5000, 3], seed=64)
+
+
+def test_many_sequences(cuda):
+    rng = np.random.default_rng(65)
+    lens = rng.integers(0, 200, size=300).tolist()
+    run_attn(cuda, 1, 2, 64, 16, int(sum(lens) // 16 + 400), orc.F16, 4, lens, seed=66)
+
+
+def test_workspace_too_small_is_flagged(cuda):
+    import torch
+    pool, rng = _pool(1, 2, 128, 16, 64, orc.BF16, 67)
+    lens = np.array([600, 300], dtype=np.int32)
+    bt, _ = block_tables(rng, lens, 16, 64)
+    q = torch.zeros((2, 8, 128), dtype=torch.bfloat16, device=cuda)
+    need = pool.attention_workspace_size(4, 2, 900)
+    small = pool.attention_workspace_size(4, 0, 256)  # room for one split only
+    assert 0 < small < need
+    ws = torch.empty(small, dtype=torch.uint8, device=cuda)
+    out = torch.full((2, 8, 128), 3.0, dtype=torch.bfloat16, device=cuda)
+    pool.decode_attention(0, q, 4, to_dev(bt), bt.shape[1], to_dev(lens), 2, 0.1, out, ws)
+    assert pool.check() & 4
+    assert (out.float() == 3.0).all()  # left unwritten
+    pool.close()
+
+
+def test_bad_block_id_flagged(cuda):
+    import torch
+    pool, rng = _pool(1, 1, 128, 16, 8, orc.BF16, 68)
+    bt = np.array([[0, 1, 99]], dtype=np.int32)
+    q = torch.zeros((1, 4, 128), dtype=torch.bfloat16, device=cuda)
+    ws = torch.empty(pool.attention_workspace_size(4, 1, 40), dtype=torch.uint8, device=cuda)
+    out = torch.empty((1, 4, 128), dtype=torch.bfloat16, device=cuda)
+    pool.decode_attention(0, q, 4, to_dev(bt), 3, to_dev(np.array([40], np.int32)), 1, 0.1, out, ws)
+    assert pool.check() & 2
+    pool.close()
+
+
+def test_bad_arguments(cuda):
+    import torch
+    q = torch.zeros(4096, dtype=torch.bfloat16, device=cuda)
+    ws = torch.empty(1 << 20, dtype=torch.uint8, device=cuda)
+    bt = to_dev(np.zeros((1, 1), np.int32))
+    ln = to_dev(np.array([1], np.int32))
+    quant = rmlx_kv.KVPool(1, 1, 128, 16, 4, dtype=orc.BF16, quant_bits=8, group_size=64)
+    with pytest.raises(rmlx_kv.RmlxError, match="quantised"):
+        quant.decode_attention(0, q, 1, bt, 1, ln, 1, 0.1, q, ws)
+    p256 = rmlx_kv.KVPool(1, 1, 256, 16, 4, dtype=orc.BF16)
+    with pytest.raises(rmlx_kv.RmlxError, match="head_dim"):
+        p256.decode_attention(0, q, 1, bt, 1, ln, 1, 0.1, q, ws)
+    p = rmlx_kv.KVPool(1, 1, 128, 16, 4, dtype=orc.BF16)
+    with pytest.raises(rmlx_kv.RmlxError, match="q_heads_per_kv"):
+        p.decode_attention(0, q, 17, bt, 1, ln, 1, 0.1, q, ws)
+    with pytest.raises(rmlx_kv.RmlxError):
+        p.decode_attention(3, q, 1, bt, 1, ln, 1, 0.1, q, ws)
+    with pytest.raises(rmlx_kv.RmlxError, match="softmax_scale"):
+        p.decode_attention(0, q, 1, bt, 1, ln, 1, 0.0, q, ws)
+    pf32 = rmlx_kv.KVPool(1, 1, 128, 16, 4, dtype=orc.F32)
+    with pytest.raises(rmlx_kv.RmlxError, match="F16 or BF16"):
+        pf32.decode_attention(0, q, 1, bt, 1, ln, 1, 0.1, q, ws)
+    for x in (quant, p256, p, pf32):
+        x.close()
