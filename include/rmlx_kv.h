@@ -392,6 +392,28 @@ RMLX_API rmlx_status rmlx_prompt_cache_save(rmlx_kv_pool* p, const int32_t* bloc
 RMLX_API rmlx_status rmlx_prompt_cache_load(rmlx_kv_pool* p, const char* path, const int32_t* block_ids, int32_t num_block_ids,
                                             int32_t* seq_len, void* stream);
 
+/* ---- Rotating (sliding-window) ring over block tables ---------------------
+ * RotatingKVCache (rotating_cache.rs:16-283) on paged blocks: a sequence of
+ * max_size ring positions keeps its first `keep` and cycles the rest; ring
+ * position p is block table entry p / block_size, row p % block_size.  The
+ * host holds the reference's (written, offset) state (rmlx_kv.batch.
+ * RotatingBlocks) and appends through slot mappings.
+ * rmlx_kv_gather_ring: get_logical_order (:162-197) of layer `layer` for
+ * num_seqs sequences: output as rmlx_kv_gather, seq_lens[s] rows; logical
+ * row i reads ring position i when ring_offsets[s] < 0 (nothing rotated, the
+ * reference's written <= max_size), else i for i < keep and
+ * keep + (ring_offsets[s] + i - keep) % (max_size - keep).  Unquantised pools.
+ * rmlx_kv_move_rows: row slot src[i] -> slot dst[i] for every layer, K and
+ * V and head (codes and scale/zero of a quantised pool), as if all were read
+ * before any is written (the shift of trim before rotation, :213-247).
+ * src/dst are device arrays; scratch of n rows is allocated on `stream`. */
+RMLX_API rmlx_status rmlx_kv_gather_ring(rmlx_kv_pool* p, int32_t layer, const int32_t* block_tables,
+                                         int32_t block_table_stride, const int32_t* seq_lens,
+                                         const int32_t* ring_offsets, int32_t num_seqs, int32_t keep, int32_t max_size,
+                                         void* out_k, void* out_v, void* stream);
+RMLX_API rmlx_status rmlx_kv_move_rows(rmlx_kv_pool* p, const int32_t* src_slots, const int32_t* dst_slots, int32_t n,
+                                       void* stream);
+
 /* Block copy for copy-on-write / fork: every tile of block src[i] is copied
  * to block dst[i] (all layers, K and V, all heads of the pool).  src/dst are
  * device arrays of n ids; the dst set must not intersect the src set.  This

@@ -153,6 +153,8 @@ _sig("rmlx_kv_attention_workspace_size", st, vp, C.c_int32, C.c_int32, C.c_int64
 _sig("rmlx_kv_decode_attention", st, vp, C.c_int32, vp, C.c_int32, vp, C.c_int32, vp, C.c_int32, C.c_float, vp, vp,
      C.c_size_t, vp)
 _sig("rmlx_kv_copy_blocks", st, vp, vp, vp, C.c_int32, vp)
+_sig("rmlx_kv_gather_ring", st, vp, C.c_int32, vp, C.c_int32, vp, vp, C.c_int32, C.c_int32, C.c_int32, vp, vp, vp)
+_sig("rmlx_kv_move_rows", st, vp, vp, vp, C.c_int32, vp)
 cpp = C.POINTER(C.c_char_p)
 _sig("rmlx_prompt_cache_write", st, C.c_char_p, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, vp,
      vp, cpp, cpp, C.c_int32)

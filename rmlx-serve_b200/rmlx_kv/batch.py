@@ -103,3 +103,90 @@ class SequenceBlocks:
 
     def seq_lens(self) -> np.ndarray:
         return np.array(self.lens, dtype=np.int32)
+
+
+class RotatingBlocks:
+    """One sliding-window sequence as a ring over its blocks: the
+    (written, offset) state machine of RotatingKVCache (rotating_cache.rs:
+    16-283) with ring position p stored in block table entry p / block_size,
+    row p % block_size.  Blocks are taken from the manager as the ring first
+    reaches them (the reference preallocates max_size rows).
+
+    The state advances once per token for all layers of the pool; the
+    reference advances it on every per-layer append call, which is the same
+    for a one-layer cache (its tests) and for each layer driven as its own
+    cache.
+    """
+
+    def __init__(self, mgr, block_size: int, max_size: int, keep: int):
+        if keep >= max_size:  # rotating_cache.rs:45-48
+            raise ValueError(f"keep ({keep}) must be less than max_size ({max_size})")
+        self.mgr, self.bs = mgr, int(block_size)
+        self.max_size, self.keep = int(max_size), int(keep)
+        self.offset = 0
+        self.written = 0
+        self.table: List[int] = []
+
+    def _slot(self, pos: int) -> int:
+        while pos // self.bs >= len(self.table):
+            bid = self.mgr.allocate()
+            if bid is None:
+                raise PoolExhausted("no free block")
+            self.table.append(int(bid))
+        return self.table[pos // self.bs] * self.bs + pos % self.bs
+
+    def append_slots(self, n: int) -> np.ndarray:
+        """Slots of n new tokens in order (append, :94-143).  A ring position
+        written twice within the call keeps the later token: the earlier
+        token's slot is -1 (skipped by rmlx_kv_append)."""
+        rotating = self.max_size - self.keep
+        slots = np.empty(n, dtype=np.int32)
+        last = {}
+        for t in range(n):
+            pos = self.written if self.written < self.max_size else self.keep + self.offset
+            slots[t] = self._slot(pos)
+            if pos in last:
+                slots[last[pos]] = -1
+            last[pos] = t
+            if self.written >= self.max_size:
+                self.offset = (self.offset + 1) % rotating
+            self.written += 1
+        return slots
+
+    def seq_len(self) -> int:  # :201-203
+        return min(self.written, self.max_size)
+
+    def can_trim(self) -> bool:  # :253-255
+        return self.seq_len() > self.keep
+
+    def ring_offset(self) -> int:
+        """For rmlx_kv_gather_ring: -1 before the ring has rotated
+        (written <= max_size), else the offset of its oldest row."""
+        return -1 if self.written <= self.max_size else self.offset
+
+    def trim(self, n: int):
+        """Drop the n oldest rows after `keep` (trim, :213-247).  Before the
+        ring rotates the rows above them shift down: returns the (src, dst)
+        slot lists that rmlx_kv_move_rows must apply; after, only the state
+        moves (empty lists)."""
+        trimmable = max(self.seq_len() - self.keep, 0)
+        if n > trimmable:
+            raise ValueError(f"cannot trim {n} tokens: only {trimmable} trimmable")
+        src, dst = [], []
+        if self.written <= self.max_size:
+            remaining = self.written - self.keep - n
+            for r in range(remaining):
+                src.append(self._slot(self.keep + n + r))
+                dst.append(self._slot(self.keep + r))
+            self.written -= n
+        else:
+            rotating = self.max_size - self.keep
+            self.offset = (self.offset + n) % rotating
+            self.written -= n
+        return np.array(src, dtype=np.int32), np.array(dst, dtype=np.int32)
+
+    def release(self) -> None:
+        for b in self.table:
+            self.mgr.free(b)
+        self.table = []
+        self.written = self.offset = 0

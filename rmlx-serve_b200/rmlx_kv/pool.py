@@ -129,6 +129,16 @@ class KVPool:
                                            block_table_stride, _ptr(seq_lens), num_seqs, softmax_scale, _ptr(out),
                                            _ptr(workspace), workspace_bytes, _stream(stream, self.device)))
 
+    def gather_ring(self, layer: int, block_tables, block_table_stride: int, seq_lens, ring_offsets, num_seqs: int,
+                    keep: int, max_size: int, out_k, out_v, stream=None) -> None:
+        """Logical-order gather of ring sequences (rotating_cache.rs:162-197)."""
+        check(lib.rmlx_kv_gather_ring(self._h, layer, _ptr(block_tables), block_table_stride, _ptr(seq_lens),
+                                      _ptr(ring_offsets), num_seqs, keep, max_size, _ptr(out_k), _ptr(out_v),
+                                      _stream(stream, self.device)))
+
+    def move_rows(self, src_slots, dst_slots, n: int, stream=None) -> None:
+        check(lib.rmlx_kv_move_rows(self._h, _ptr(src_slots), _ptr(dst_slots), n, _stream(stream, self.device)))
+
     def copy_blocks(self, src, dst, n: int, stream=None) -> None:
         check(lib.rmlx_kv_copy_blocks(self._h, _ptr(src), _ptr(dst), n, _stream(stream, self.device)))
 
