@@ -352,6 +352,44 @@ RMLX_API rmlx_status rmlx_kv_decode_attention(rmlx_kv_pool* p, int32_t layer, co
                                               const int32_t* seq_lens, int32_t num_seqs, float softmax_scale, void* out,
                                               void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- Batch block tables (the scheduler's KV bookkeeping) -----------------
+ * Replaces the per-sequence KVCache / BatchKVCache slots of the scheduler
+ * (scheduler.rs:281-436, batch_generator.rs:404-481, 602-630) with block
+ * tables over a PagedCacheManager, optionally with a PrefixCacheManager (the
+ * scheduler's prefix cache, never set in the reference, scheduler.rs:168-172).
+ * No counterpart in the crate itself; the policy is in kv_batch.cc.
+ *   add: admits a prompt into the lowest free row; *cached_tokens leading
+ *        prompt tokens already sit in reused prefix-cache blocks (prefill may
+ *        skip them); slots[0 .. n - cached) are the slots of the rest.
+ *        RMLX_E_EXHAUSTED when no row or no block can be had.
+ *   step: one token per listed sequence: slots[i] for uids[i]; cow_src/dst
+ *        (capacity n) the tiles to copy with rmlx_kv_copy_blocks before the
+ *        append.  All-or-nothing: RMLX_E_EXHAUSTED leaves the tables as they
+ *        were.
+ *   fork / remove (cache_prefix: the finished sequence's full blocks go to
+ *        the prefix cache first).
+ *   tables: rows [0, *num_rows) as block_tables[row][stride] (0-padded) and
+ *        seq_lens[row] (0 for a free row); both NULL = size query.
+ * The batch holds references in the block manager: destroy it first. */
+typedef struct rmlx_kv_batch rmlx_kv_batch;
+typedef struct {
+  uint64_t admitted, rejected, prompt_tokens, cached_tokens, new_blocks, evictions, cow_copies;
+} rmlx_batch_stats;
+RMLX_API rmlx_status rmlx_kv_batch_new(rmlx_block_manager* m, rmlx_prefix_cache* prefix, int32_t max_seqs,
+                                       rmlx_kv_batch** out);
+RMLX_API void rmlx_kv_batch_destroy(rmlx_kv_batch* b);
+RMLX_API rmlx_status rmlx_kv_batch_add(rmlx_kv_batch* b, uint64_t uid, const uint32_t* prompt, int32_t n, int32_t* row,
+                                       int32_t* cached_tokens, int32_t* slots);
+RMLX_API rmlx_status rmlx_kv_batch_fork(rmlx_kv_batch* b, uint64_t parent_uid, uint64_t child_uid, int32_t* row);
+RMLX_API rmlx_status rmlx_kv_batch_remove(rmlx_kv_batch* b, uint64_t uid, int32_t cache_prefix);
+RMLX_API rmlx_status rmlx_kv_batch_step(rmlx_kv_batch* b, const uint64_t* uids, const uint32_t* tokens, int32_t n,
+                                        int32_t* slots, int32_t* cow_src, int32_t* cow_dst, int32_t* n_cow);
+RMLX_API rmlx_status rmlx_kv_batch_tables(const rmlx_kv_batch* b, int32_t* block_tables, int32_t stride,
+                                          int32_t* seq_lens, int32_t max_rows, int32_t* num_rows, int32_t* max_blocks);
+RMLX_API rmlx_status rmlx_kv_batch_seq(const rmlx_kv_batch* b, uint64_t uid, int32_t* row, int32_t* len,
+                                       int32_t* block_ids, int32_t cap, int32_t* nblocks);
+RMLX_API void rmlx_kv_batch_stats(const rmlx_kv_batch* b, rmlx_batch_stats* out);
+
 /* ---- Prompt cache files (prompt_cache.rs:63-210) --------------------------
  * A sequence's K/V as a safetensors file: one [seq_len, head_dim] tensor per
  * (layer, head) named layer_{l}_head_{h}_keys / layer_{l}_head_{h}_values

@@ -675,6 +675,18 @@ size_t orc_prefix_lookup(void* p, const uint32_t* t, size_t n, size_t* out, size
 void orc_prefix_insert(void* p, const uint32_t* t, size_t n, const size_t* ids, size_t nb) {
   ((PrefixCache*)p)->insert(t, n, ids, nb);
 }
+// insert, reporting per block whether its node had no block (attached[i] = 1)
+// and the block it replaced (replaced[i], -1 for none)
+void orc_prefix_insert_report(void* p, const uint32_t* t, size_t n, const size_t* ids, size_t nb, int32_t* attached,
+                              int64_t* replaced) {
+  std::vector<int> a;
+  std::vector<long long> r;
+  ((PrefixCache*)p)->insert_report(t, n, ids, nb, &a, &r);
+  for (size_t i = 0; i < nb; ++i) {
+    attached[i] = a[i];
+    replaced[i] = r[i];
+  }
+}
 int orc_prefix_evict_lru(void* p, size_t* out) { return ((PrefixCache*)p)->evict_lru(out) ? 1 : 0; }
 double orc_prefix_hit_rate(void* p) { return ((PrefixCache*)p)->hit_rate(); }
 size_t orc_prefix_num_blocks(void* p) { return ((PrefixCache*)p)->num_blocks; }
@@ -1090,7 +1102,10 @@ int orc_prefix_admit(void* mv, void* pv, const uint32_t* tokens, const int64_t* 
       std::vector<size_t> full(ids, ids + nfull);
       p->insert_report(t, (size_t)(nfull * bs), full.data(), (size_t)nfull, &attached, &replaced);
       for (int64_t b = 0; b < nfull; ++b) {
-        if (attached[b]) m->increment_ref((size_t)ids[b]);
+        // the cache holds one reference on every block it holds: a block it
+        // starts holding (new node block, or one that replaces another) gains
+        // one, a block it stops holding loses one
+        if (attached[b] || replaced[b] >= 0) m->increment_ref((size_t)ids[b]);
         if (replaced[b] >= 0) m->free_block((size_t)replaced[b]);
       }
     }

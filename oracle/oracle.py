@@ -63,6 +63,7 @@ _sig("orc_prefix_delete", None, vp)
 _sig("orc_prefix_lookup", sz, vp, u32p, sz, szp, sz)
 _sig("orc_prefix_insert", None, vp, u32p, sz, szp, sz)
 _sig("orc_prefix_evict_lru", C.c_int, vp, szp)
+_sig("orc_prefix_insert_report", None, vp, u32p, sz, szp, sz, C.POINTER(C.c_int32), i64p)
 _sig("orc_prefix_hit_rate", C.c_double, vp)
 _sig("orc_prefix_num_blocks", sz, vp)
 _sig("orc_prefix_num_nodes", sz, vp)
@@ -208,6 +209,16 @@ class PrefixCacheManager:
     def insert(self, toks, ids):
         a, b = _a(toks, np.uint32), _a(ids, np.uint64)
         _l.orc_prefix_insert(self._h, _p(a, u32p), len(a), _p(b, szp), len(b))
+
+    def insert_report(self, toks, ids):
+        """insert, returning (attached, replaced) per block."""
+        t = _a(toks, np.uint32) if len(toks) else np.zeros(1, np.uint32)
+        b = _a(ids, np.uint64).view(np.uintp) if len(ids) else np.zeros(1, np.uintp)
+        att = np.zeros(max(len(ids), 1), np.int32)
+        rep = np.zeros(max(len(ids), 1), np.int64)
+        _l.orc_prefix_insert_report(self._h, _p(t, u32p), len(toks), _p(b, szp), len(ids),
+                                    att.ctypes.data_as(C.POINTER(C.c_int32)), _p(rep, i64p))
+        return att[:len(ids)], rep[:len(ids)]
 
     def evict_lru(self) -> Optional[int]:
         o = sz()

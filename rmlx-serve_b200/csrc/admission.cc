@@ -17,8 +17,9 @@
 //     references are released, its block ids reported as -1);
 //  4. new blocks get their token ids, full ones their hash;
 //  5. the full-block prefix is inserted into the prefix cache, which takes a
-//     reference on every block it newly holds (and drops the one it held on
-//     a block it replaces);
+//     reference on every block it starts holding (at a node that had none,
+//     or in place of another block) and drops the one it held on a block it
+//     replaces;
 //  6. the request releases its own references (prefill-only admission: what
 //     stays allocated is exactly what the prefix cache holds).
 #include <new>
@@ -111,7 +112,7 @@ extern "C" rmlx_status rmlx_prefix_admit(rmlx_block_manager* mh, rmlx_prefix_cac
       replaced.assign((size_t)nfull, -1);
       p.insert_report(t, (size_t)(nfull * bs), ids, (size_t)nfull, attached.data(), replaced.data());
       for (int64_t b = 0; b < nfull; ++b) {
-        if (attached[b]) m.increment_ref(ids[b]);
+        if (attached[b] || replaced[b] >= 0) m.increment_ref(ids[b]);
         if (replaced[b] >= 0) m.free_block(replaced[b]);
       }
     }

@@ -153,6 +153,23 @@ _sig("rmlx_kv_attention_workspace_size", st, vp, C.c_int32, C.c_int32, C.c_int64
 _sig("rmlx_kv_decode_attention", st, vp, C.c_int32, vp, C.c_int32, vp, C.c_int32, vp, C.c_int32, C.c_float, vp, vp,
      C.c_size_t, vp)
 _sig("rmlx_kv_copy_blocks", st, vp, vp, vp, C.c_int32, vp)
+
+
+class BatchStats(C.Structure):
+    _fields_ = [(n, C.c_uint64) for n in ("admitted", "rejected", "prompt_tokens", "cached_tokens", "new_blocks",
+                                          "evictions", "cow_copies")]
+
+
+u64p = C.POINTER(C.c_uint64)
+_sig("rmlx_kv_batch_new", st, vp, vp, C.c_int32, C.POINTER(vp))
+_sig("rmlx_kv_batch_destroy", None, vp)
+_sig("rmlx_kv_batch_add", st, vp, C.c_uint64, u32p, C.c_int32, i32p, i32p, i32p)
+_sig("rmlx_kv_batch_fork", st, vp, C.c_uint64, C.c_uint64, i32p)
+_sig("rmlx_kv_batch_remove", st, vp, C.c_uint64, C.c_int32)
+_sig("rmlx_kv_batch_step", st, vp, u64p, u32p, C.c_int32, i32p, i32p, i32p, i32p)
+_sig("rmlx_kv_batch_tables", st, vp, i32p, C.c_int32, i32p, C.c_int32, i32p, i32p)
+_sig("rmlx_kv_batch_seq", st, vp, C.c_uint64, i32p, i32p, i32p, C.c_int32, i32p)
+_sig("rmlx_kv_batch_stats", None, vp, C.POINTER(BatchStats))
 _sig("rmlx_kv_gather_ring", st, vp, C.c_int32, vp, C.c_int32, vp, vp, C.c_int32, C.c_int32, C.c_int32, vp, vp, vp)
 _sig("rmlx_kv_move_rows", st, vp, vp, vp, C.c_int32, vp)
 cpp = C.POINTER(C.c_char_p)

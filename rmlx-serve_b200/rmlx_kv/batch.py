@@ -18,9 +18,12 @@ or the oracle's restatement in the tests).
 """
 from __future__ import annotations
 
+import ctypes as C
 from typing import List, Sequence, Tuple
 
 import numpy as np
+
+from . import _lib
 
 
 class PoolExhausted(RuntimeError):
@@ -190,3 +193,87 @@ class RotatingBlocks:
             self.mgr.free(b)
         self.table = []
         self.written = self.offset = 0
+
+
+class KVBatch:
+    """The scheduler's KV bookkeeping on block tables (rmlx_kv_batch_* in
+    the C ABI): admit prompts (reusing prefix-cache blocks), one token per
+    sequence per step (with copy-on-write of shared tails), forks, removal
+    (optionally into the prefix cache), and the dense block tables and
+    lengths a step's device calls take."""
+
+    def __init__(self, mgr, prefix=None, max_seqs: int = 256):
+        h = _lib.vp()
+        _lib.check(_lib.lib.rmlx_kv_batch_new(mgr._h, prefix._h if prefix is not None else None, max_seqs,
+                                              C.byref(h)))
+        self._h, self._mgr, self._prefix, self.max_seqs = h, mgr, prefix, max_seqs
+        mgr._dependents.add(self)
+        if prefix is not None:
+            prefix._dependents.add(self)
+
+    def __del__(self):
+        self.close()
+
+    def close(self):
+        if getattr(self, "_h", None):
+            _lib.lib.rmlx_kv_batch_destroy(self._h)
+            self._h = None
+
+    def add(self, uid: int, prompt: Sequence[int]):
+        """-> (row, cached_tokens, slots of the uncached prompt tokens)."""
+        p = np.ascontiguousarray(np.asarray(prompt, dtype=np.uint32))
+        slots = np.empty(max(len(p), 1), dtype=np.int32)
+        row, cached = C.c_int32(), C.c_int32()
+        _lib.check(_lib.lib.rmlx_kv_batch_add(self._h, uid, p.ctypes.data_as(_lib.u32p), len(p), C.byref(row),
+                                              C.byref(cached), slots.ctypes.data_as(_lib.i32p)))
+        return row.value, cached.value, slots[:len(p) - cached.value]
+
+    def fork(self, parent: int, child: int) -> int:
+        row = C.c_int32()
+        _lib.check(_lib.lib.rmlx_kv_batch_fork(self._h, parent, child, C.byref(row)))
+        return row.value
+
+    def remove(self, uid: int, cache_prefix: bool = False) -> None:
+        _lib.check(_lib.lib.rmlx_kv_batch_remove(self._h, uid, int(cache_prefix)))
+
+    def step(self, uids: Sequence[int], tokens: Sequence[int]):
+        """-> (slots, cow_src, cow_dst) for one token per listed sequence."""
+        u = np.ascontiguousarray(np.asarray(uids, dtype=np.uint64))
+        t = np.ascontiguousarray(np.asarray(tokens, dtype=np.uint32))
+        if len(u) != len(t):
+            raise ValueError("one token per sequence")
+        n = len(u)
+        slots = np.empty(max(n, 1), np.int32)
+        src = np.empty(max(n, 1), np.int32)
+        dst = np.empty(max(n, 1), np.int32)
+        nc = C.c_int32()
+        _lib.check(_lib.lib.rmlx_kv_batch_step(self._h, u.ctypes.data_as(C.POINTER(C.c_uint64)),
+                                               t.ctypes.data_as(_lib.u32p), n, slots.ctypes.data_as(_lib.i32p),
+                                               src.ctypes.data_as(_lib.i32p), dst.ctypes.data_as(_lib.i32p),
+                                               C.byref(nc)))
+        return slots[:n], src[:nc.value], dst[:nc.value]
+
+    def tables(self):
+        """-> (block_tables [rows, max_blocks] int32, seq_lens [rows] int32)."""
+        nr, mb = C.c_int32(), C.c_int32()
+        _lib.check(_lib.lib.rmlx_kv_batch_tables(self._h, None, 0, None, 0, C.byref(nr), C.byref(mb)))
+        bt = np.zeros((max(nr.value, 1), max(mb.value, 1)), np.int32)
+        lens = np.zeros(max(nr.value, 1), np.int32)
+        _lib.check(_lib.lib.rmlx_kv_batch_tables(self._h, bt.ctypes.data_as(_lib.i32p), bt.shape[1],
+                                                 lens.ctypes.data_as(_lib.i32p), bt.shape[0], C.byref(nr),
+                                                 C.byref(mb)))
+        return bt[:nr.value, :mb.value], lens[:nr.value]
+
+    def seq(self, uid: int):
+        """-> (row, length, block ids) of one sequence."""
+        row, ln, nb = C.c_int32(), C.c_int32(), C.c_int32()
+        _lib.check(_lib.lib.rmlx_kv_batch_seq(self._h, uid, C.byref(row), C.byref(ln), None, 0, C.byref(nb)))
+        ids = np.zeros(max(nb.value, 1), np.int32)
+        _lib.check(_lib.lib.rmlx_kv_batch_seq(self._h, uid, C.byref(row), C.byref(ln), ids.ctypes.data_as(_lib.i32p),
+                                              len(ids), C.byref(nb)))
+        return row.value, ln.value, ids[:nb.value]
+
+    def stats(self) -> dict:
+        s = _lib.BatchStats()
+        _lib.lib.rmlx_kv_batch_stats(self._h, s)
+        return {n: getattr(s, n) for n, _ in s._fields_}

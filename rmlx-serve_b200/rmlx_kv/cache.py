@@ -8,6 +8,7 @@ reference's panic message.
 from __future__ import annotations
 
 import ctypes as C
+import weakref
 from dataclasses import dataclass
 from typing import List, Optional, Sequence
 
@@ -51,9 +52,12 @@ class PagedCacheManager:
         check(lib.rmlx_block_manager_new(block_size, num_blocks, C.byref(h)))
         self._h = h
         self._bs = block_size
+        self._dependents = weakref.WeakSet()  # objects holding references in this manager
 
     def __del__(self):
         if getattr(self, "_h", None):
+            for d in list(getattr(self, "_dependents", ())):
+                d.close()  # a batch releases its references before the manager goes
             lib.rmlx_block_manager_destroy(self._h)
             self._h = None
 
@@ -132,9 +136,12 @@ class PrefixCacheManager:
         h = _lib.vp()
         check(lib.rmlx_prefix_cache_new(max_blocks, C.byref(h)))
         self._h = h
+        self._dependents = weakref.WeakSet()
 
     def __del__(self):
         if getattr(self, "_h", None):
+            for d in list(getattr(self, "_dependents", ())):
+                d.close()
             lib.rmlx_prefix_cache_destroy(self._h)
             self._h = None
 
