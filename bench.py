@@ -872,20 +872,21 @@ def main():
         return
 
     # ---- e2e: the same steps through the public API with host buffers ----
-    # Per step: block-manager allocation for sequences crossing a block
-    # boundary, H2D of the new K/V (pinned), slots, block tables and lengths,
-    # the append and the per-layer gathers, and a D2H read of the step's
-    # status word.  The gathered K/V stay in HBM for the attention that
-    # consumes them.
+    # Per step: the batch planner (rmlx_kv_batch_step) gives each sequence's
+    # slot, new blocks and block tables; H2D of the new K/V (pinned), slots,
+    # block tables and lengths; the append and the per-layer gathers (or
+    # attention); a D2H read of the step's status word.  The gathered K/V stay
+    # in HBM for the attention that consumes them.
+    from rmlx_kv.batch import KVBatch
     mgr = rmlx_kv.PagedCacheManager(BS, num_blocks)
     rng = np.random.default_rng(w.seed + 7)
     mgr.free_n(rng.permutation(mgr.allocate_n(num_blocks)))
+    planner = KVBatch(mgr, None, B)
+    uids = np.arange(1, B + 1, dtype=np.uint64)
+    for s in range(B):  # prompts as long as the sequences are when the timed steps start
+        planner.add(int(uids[s]), rng.integers(0, 128256, size=int(lens0[s]) + W, dtype=np.uint32))
+    step_tokens = rng.integers(0, 128256, size=(K, B), dtype=np.uint32)
     host_bt = np.zeros_like(bt)
-    nblk = np.zeros(B, dtype=np.int64)
-    for s in range(B):
-        n0 = (int(lens0[s]) + BS - 1) // BS
-        host_bt[s, :n0] = mgr.allocate_n(n0)
-        nblk[s] = n0
     pin_k = torch.empty((K, L, B, H, D), dtype=torch.bfloat16, pin_memory=True)
     pin_v = torch.empty_like(pin_k, pin_memory=True)
     pin_k.copy_(new_k[W:W + K].cpu())
@@ -908,14 +909,11 @@ def main():
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     for i in range(K):
-        lens_np, sl, btn = pin_lens.numpy(), pin_slots.numpy(), pin_bt.numpy()
-        for s in range(B):
-            p = int(lens0[s]) + W + i  # position written this step
-            while p // BS >= nblk[s]:
-                btn[s, nblk[s]] = mgr.allocate_n(1)[0]
-                nblk[s] += 1
-            sl[s] = btn[s, p // BS] * BS + p % BS
-            lens_np[s] = p + 1
+        slots_i, _, _ = planner.step(uids, step_tokens[i])
+        tb, ln = planner.tables()
+        pin_slots.numpy()[:] = slots_i
+        pin_lens.numpy()[:] = ln
+        pin_bt.numpy()[:, :tb.shape[1]] = tb
         dk.copy_(pin_k[i], non_blocking=True)
         dv.copy_(pin_v[i], non_blocking=True)
         d_slots.copy_(pin_slots, non_blocking=True)
@@ -968,6 +966,7 @@ def main():
             "cpu_baseline": cpu,
             "clocks": clk,
         }), flush=True)
+    planner.close()
     pool.close()
     if dist is not None:
         dist.barrier()
