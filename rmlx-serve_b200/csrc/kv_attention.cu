@@ -8,14 +8,15 @@
 //
 // Split over the sequence (flash-decoding): a work item is (split of 256
 // tokens, KV head), one warp per item.  A warp streams its split in chunks of
-// 16 tokens through shared memory (cp.async, three stages per warp) and runs
+// 16 tokens through shared memory (cp.async, two stages per warp) and runs
 // both products on the tensor cores with mma.sync m16n8k16 (f16/bf16 inputs,
 // f32 accumulation): S = Q K^T with the G query heads as the M rows, then
 // O += P V with P (the exponentiated scores, rounded to the pool's type) as
 // the A operand.  An online softmax in the log2 domain keeps a running max
-// and sum per query head.  Each item writes its unnormalised O, max and sum
-// to a workspace; a second kernel combines the splits of each (sequence,
-// query head) and writes the output in the pool's type.
+// and sum per query head.  A sequence held by one item is normalised and
+// written directly; otherwise each item writes its unnormalised O, max and
+// sum to a workspace, and a second kernel combines the splits of each
+// (sequence, query head) and writes the output in the pool's type.
 //
 // The kernel is HBM-bound: per token and KV head it reads 2 x head_dim x 2
 // bytes and does 4 x G x head_dim flops (G = 4..8: 8..16 flops per byte),
@@ -33,7 +34,6 @@ namespace rmlx {
 
 constexpr int ATT_SPLIT = 256;  // tokens per work item
 constexpr int ATT_CHUNK = 16;   // tokens per tensor-core step
-constexpr int ATT_STAGES = 3;   // chunks in flight per warp
 constexpr int ATT_WARPS = 4;    // warps per CTA (independent items)
 
 __device__ __forceinline__ float ex2(float x) {
@@ -90,15 +90,85 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   }
 }
 
+// Combine the splits of sequence s for query head j of KV head h: n splits
+// starting at global split `base` (items (base + i) * heads + h), written as
+// out[s][h * G + j][:] in the pool's type.  Splits are taken 16 at a time:
+// their (max, sum) pairs one per lane, and every lane's head_dim / 32
+// elements of the 16 partial outputs, all loaded before any arithmetic, so a
+// round costs one memory latency; weights reach the lanes by shuffle and an
+// online max carries across rounds.
+template <int DT, int HD>
+__device__ __forceinline__ void combine_splits(const float* part_o, const float* part_ml, uint8_t* out, int s,
+                                               int h, int j, int G, int heads, int base, int n, int lane) {
+  constexpr int EPL = HD / 32;
+  constexpr int R = 16;
+  constexpr unsigned FULL = 0xffffffffu;
+  const float2* ml = reinterpret_cast<const float2*>(part_ml) + ((int64_t)base * heads + h) * G + j;
+  const int64_t mstride = (int64_t)heads * G;
+  const float* po = part_o + (((int64_t)base * heads + h) * G + j) * HD + lane * EPL;
+  const int64_t ostride = (int64_t)heads * G * HD;
+  float mx = -INFINITY, L = 0.0f, acc[EPL];
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) acc[e] = 0.0f;
+  for (int r0 = 0; r0 < n; r0 += R) {
+    const int cnt = min(R, n - r0);
+    float2 mlv = make_float2(-INFINITY, 0.0f);
+    if (lane < cnt) mlv = __ldcg(ml + (int64_t)(r0 + lane) * mstride);
+    float vv[R][EPL];
+#pragma unroll
+    for (int k = 0; k < R; ++k) {
+      const float* pk = po + (int64_t)(r0 + k) * ostride;
+#pragma unroll
+      for (int e = 0; e < EPL; e += 2) {
+        float2 x = make_float2(0.0f, 0.0f);
+        if (k < cnt) x = __ldcg(reinterpret_cast<const float2*>(pk + e));
+        vv[k][e] = x.x;
+        vv[k][e + 1] = x.y;
+      }
+    }
+    float cm = mlv.x;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) cm = fmaxf(cm, __shfl_xor_sync(FULL, cm, o));
+    const float nm = fmaxf(mx, cm);
+    const float a = ex2(mx - nm);
+    L *= a;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) acc[e] *= a;
+    mx = nm;
+    const float wl = lane < cnt ? ex2(mlv.x - nm) : 0.0f;
+    L += mlv.y * wl;
+#pragma unroll
+    for (int k = 0; k < R; ++k) {
+      const float w = __shfl_sync(FULL, wl, k);
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) acc[e] += w * vv[k][e];
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(FULL, L, o);
+  const float inv = 1.0f / L;
+  uint32_t wv[EPL / 2];
+#pragma unroll
+  for (int e = 0; e < EPL; e += 2) wv[e / 2] = pack2<DT>(acc[e] * inv, acc[e + 1] * inv);
+  uint8_t* dst = out + ((int64_t)s * heads * G + (int64_t)h * G + j) * HD * 2 + lane * EPL * 2;
+  if (EPL == 4) *reinterpret_cast<uint2*>(dst) = make_uint2(wv[0], wv[1]);
+  else *reinterpret_cast<uint32_t*>(dst) = wv[0];
+}
+
 // Shared-memory layout of one stage: K rows then V rows of a 16-token chunk,
 // row-major, 16-byte column chunk c of row r stored at slot c ^ (r & 7) so
 // that the 8 row addresses of every ldmatrix hit 8 different bank groups.
-template <int DT, int HD>
-__global__ void __launch_bounds__(ATT_WARPS * 32, 2)
+// STAGES chunks are in flight per warp; MINB CTAs per SM; QSMEM keeps the
+// queries in shared memory (same layout, 16 rows) and reads their A
+// fragments with ldmatrix at every step instead of holding them in
+// registers.  `split` tokens per work item (a multiple of 16).
+template <int DT, int HD, int STAGES, int MINB, bool QSMEM>
+__global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
     paged_decode_attn_kernel(PoolGeo g, int layer, const uint8_t* __restrict__ q, int G,
                              const int32_t* __restrict__ bt, int bt_stride, const int32_t* __restrict__ lens,
-                             int nseq, float scale_log2, float* __restrict__ part_o, float* __restrict__ part_ml,
-                             int64_t cap_splits, int32_t* err) {
+                             int nseq, int split, float scale_log2, float* __restrict__ part_o,
+                             float* __restrict__ part_ml, int64_t cap_splits, uint8_t* __restrict__ out,
+                             int32_t* err) {
   constexpr int ROWB = HD * 2;  // bytes of one K or V row
   constexpr int CPR = ROWB / 16;
   constexpr int KT = HD / 16;  // k-steps of S = Q K^T
@@ -110,10 +180,12 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, 2)
   int32_t* cut = cub + nseq + 1;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const size_t scan_bytes = ((size_t)2 * (nseq + 1) * 4 + 127) & ~(size_t)127;
-  const uint32_t wbuf = (uint32_t)__cvta_generic_to_shared(smem + scan_bytes) + warp * ATT_STAGES * STAGE;
+  constexpr int WBYTES = STAGES * STAGE + (QSMEM ? ATT_CHUNK * ROWB : 0);  // per warp
+  const uint32_t wbuf = (uint32_t)__cvta_generic_to_shared(smem + scan_bytes) + warp * WBYTES;
+  const uint32_t qbuf = wbuf + STAGES * STAGE;
   pdl_wait();
   pdl_release();
-  scan_seq_lens(lens, nseq, ATT_SPLIT, cub, cut);
+  scan_seq_lens(lens, nseq, split, cub, cut);
   const int64_t nsplit = cub[nseq];
   if (nsplit > cap_splits) {
     if (threadIdx.x == 0) atomicOr(err, DEV_ERR_WORKSPACE);
@@ -121,6 +193,12 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, 2)
   }
   const int64_t items = nsplit * g.heads;
   const int qheads = g.heads * G;
+  // sequences of length 0 have no split: their outputs are zeros
+  for (int64_t s0 = (int64_t)blockIdx.x * ATT_WARPS + warp; s0 < nseq; s0 += (int64_t)gridDim.x * ATT_WARPS)
+    if (cut[s0 + 1] == cut[s0]) {
+      uint4* o4 = reinterpret_cast<uint4*>(out + s0 * qheads * ROWB);
+      for (int x = lane; x < qheads * CPR; x += 32) o4[x] = make_uint4(0u, 0u, 0u, 0u);
+    }
   const int r = lane >> 2, c = lane & 3;
   const int64_t vdelta = (int64_t)g.heads * g.tile_bytes;  // V tile of (block, layer, head) after its K tile
   const bool aligned_blocks = (g.bs % ATT_CHUNK) == 0;     // a chunk never crosses a block
@@ -130,24 +208,39 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, 2)
     const int h = (int)(it % g.heads);
     const int64_t sg = it / g.heads;
     const int s = find_seq(cub, nseq, sg);
-    const int t_begin = (int)(sg - cub[s]) * ATT_SPLIT;
-    const int t_end = min(cut[s + 1] - cut[s], t_begin + ATT_SPLIT);
+    const int t_begin = (int)(sg - cub[s]) * split;
+    const int t_end = min(cut[s + 1] - cut[s], t_begin + split);
     const int nchunks = (t_end - t_begin + ATT_CHUNK - 1) / ATT_CHUNK;
     const int32_t* btrow = bt + (int64_t)s * bt_stride;
 
-    // Q as A fragments (rows = query heads, zero beyond G).
-    uint32_t qa[KT][4];
+    // Q as A fragments (rows = query heads, zero beyond G): in registers,
+    // or staged in shared memory for ldmatrix at every step.
+    uint32_t qa[QSMEM ? 1 : KT][4];
     const uint8_t* qbase = q + ((int64_t)s * qheads + (int64_t)h * G) * ROWB;
+    if (QSMEM) {
 #pragma unroll
-    for (int kk = 0; kk < KT; ++kk)
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int row = r + (i & 1) * 8, col = kk * 16 + 2 * c + (i >> 1) * 8;
-        qa[kk][i] = row < G ? __ldg(reinterpret_cast<const uint32_t*>(qbase + (int64_t)row * ROWB + col * 2)) : 0u;
+      for (int i = 0; i < (ATT_CHUNK * CPR) / 32; ++i) {
+        const int idx = lane + 32 * i, row = idx / CPR, ch = idx % CPR;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (row < G) v = __ldg(reinterpret_cast<const uint4*>(qbase + (int64_t)row * ROWB + ch * 16));
+        const uint32_t a = qbuf + row * ROWB + ((ch ^ (row & 7)) << 4);
+        asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                     : "memory");
       }
+      __syncwarp();
+    } else {
+#pragma unroll
+      for (int kk = 0; kk < KT; ++kk)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int row = r + (i & 1) * 8, col = kk * 16 + 2 * c + (i >> 1) * 8;
+          qa[kk][i] =
+              row < G ? __ldg(reinterpret_cast<const uint32_t*>(qbase + (int64_t)row * ROWB + col * 2)) : 0u;
+        }
+    }
 
     auto load_chunk = [&](int ci) {
-      const uint32_t dst = wbuf + (ci % ATT_STAGES) * STAGE;
+      const uint32_t dst = wbuf + (ci % STAGES) * STAGE;
       const int tc = t_begin + ci * ATT_CHUNK;
       if (aligned_blocks) {
         // the chunk's 16 rows are contiguous in one K tile (and one V tile)
@@ -198,16 +291,16 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, 2)
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;  // rows r and r + 8
 
 #pragma unroll
-    for (int ci = 0; ci < ATT_STAGES - 1; ++ci) {
+    for (int ci = 0; ci < STAGES - 1; ++ci) {
       if (ci < nchunks) load_chunk(ci);
       else cp_async_commit();  // keep one group per slot so the wait count stays fixed
     }
     for (int ci = 0; ci < nchunks; ++ci) {
-      if (ci + ATT_STAGES - 1 < nchunks) load_chunk(ci + ATT_STAGES - 1);
+      if (ci + STAGES - 1 < nchunks) load_chunk(ci + STAGES - 1);
       else cp_async_commit();
-      cp_async_wait<ATT_STAGES - 1>();
+      cp_async_wait<STAGES - 1>();
       __syncwarp();
-      const uint32_t kb = wbuf + (ci % ATT_STAGES) * STAGE, vb = kb + ATT_CHUNK * ROWB;
+      const uint32_t kb = wbuf + (ci % STAGES) * STAGE, vb = kb + ATT_CHUNK * ROWB;
       const int tc = t_begin + ci * ATT_CHUNK;
 
       // S = Q K^T: two n-tiles of 8 tokens
@@ -217,8 +310,16 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, 2)
         const int mi = lane >> 3, row = ((mi >> 1) << 3) + (lane & 7), ch = 2 * kk + (mi & 1);
         uint32_t b0, b1, b2, b3;
         ldsm_x4(kb + row * ROWB + ((ch ^ (row & 7)) << 4), b0, b1, b2, b3);
-        mma16816<DT>(sacc[0], qa[kk], b0, b1);
-        mma16816<DT>(sacc[1], qa[kk], b2, b3);
+        if (QSMEM) {
+          // A fragment: matrices (rows 0-7 | 8-15) x (k 0-7 | 8-15) of step kk
+          const int qrow = ((mi & 1) << 3) + (lane & 7), qch = 2 * kk + (mi >> 1);
+          ldsm_x4(qbuf + qrow * ROWB + ((qch ^ (qrow & 7)) << 4), qa[0][0], qa[0][1], qa[0][2], qa[0][3]);
+          mma16816<DT>(sacc[0], qa[0], b0, b1);
+          mma16816<DT>(sacc[1], qa[0], b2, b3);
+        } else {
+          mma16816<DT>(sacc[0], qa[kk], b0, b1);
+          mma16816<DT>(sacc[1], qa[kk], b2, b3);
+        }
       }
       // online softmax (log2 domain), masking tokens past the split's end
       float mx0 = -INFINITY, mx1 = -INFINITY;
@@ -284,6 +385,18 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, 2)
     l0 += __shfl_xor_sync(FULL, l0, 2);
     l1 += __shfl_xor_sync(FULL, l1, 1);
     l1 += __shfl_xor_sync(FULL, l1, 2);
+    const int nsp = cub[s + 1] - cub[s];
+    if (nsp == 1) {  // the whole sequence in this item: normalise and write the output
+      const float i0 = 1.0f / l0, i1 = 1.0f / l1;
+      uint8_t* ob = out + ((int64_t)s * qheads + (int64_t)h * G) * ROWB;
+#pragma unroll
+      for (int d = 0; d < NT; ++d) {
+        if (r < G) *reinterpret_cast<uint32_t*>(ob + r * ROWB + (8 * d + 2 * c) * 2) = pack2<DT>(o[d][0] * i0, o[d][1] * i0);
+        if (r + 8 < G)
+          *reinterpret_cast<uint32_t*>(ob + (r + 8) * ROWB + (8 * d + 2 * c) * 2) = pack2<DT>(o[d][2] * i1, o[d][3] * i1);
+      }
+      continue;
+    }
     float* po = part_o + it * (int64_t)G * HD;
     float* pml = part_ml + it * (int64_t)2 * G;
 #pragma unroll
@@ -298,54 +411,31 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, 2)
   }
 }
 
-// One warp per (sequence, query head): combine the splits' (O, max, sum) and
-// write out[s][qh][:] in the pool's type.  A sequence of length 0 gets zeros.
+// One warp per (sequence, query head) of the sequences held by two or more
+// splits (the split kernel wrote the others): combine_splits.
 template <int DT, int HD>
-__global__ void __launch_bounds__(256) attn_combine_kernel(const int32_t* __restrict__ lens, int nseq, int heads, int G,
-                                                           const float* __restrict__ part_o,
+__global__ void __launch_bounds__(256) attn_combine_kernel(const int32_t* __restrict__ lens, int nseq, int split,
+                                                           int heads, int G, const float* __restrict__ part_o,
                                                            const float* __restrict__ part_ml, uint8_t* __restrict__ out,
                                                            int64_t cap_splits) {
-  constexpr int EPL = HD / 32;  // elements per lane
   extern __shared__ int32_t cs[];
   int32_t* cub = cs;
   int32_t* cut = cs + nseq + 1;
-  pdl_wait();
+  // seq_lens is an input of the split kernel, not one of its outputs: the
+  // scan may run while that kernel drains; the partials are read after the wait
   pdl_release();
-  scan_seq_lens(lens, nseq, ATT_SPLIT, cub, cut);
+  scan_seq_lens(lens, nseq, split, cub, cut);
+  pdl_wait();
   if (cub[nseq] > cap_splits) return;  // flagged by the split kernel
   const int lane = threadIdx.x & 31;
   const int qheads = heads * G;
   const int64_t total = (int64_t)nseq * qheads;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   for (int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; w < total; w += nwarps) {
-    const int s = (int)(w / qheads), qh = (int)(w % qheads), h = qh / G, j = qh % G;
+    const int s = (int)(w / qheads), qh = (int)(w % qheads);
     const int n = cub[s + 1] - cub[s];
-    float mx = -INFINITY;
-    for (int i = 0; i < n; ++i) mx = fmaxf(mx, __ldg(part_ml + ((int64_t)(cub[s] + i) * heads + h) * 2 * G + 2 * j));
-    float acc[EPL];
-#pragma unroll
-    for (int e = 0; e < EPL; ++e) acc[e] = 0.0f;
-    float L = 0.0f;
-    for (int i = 0; i < n; ++i) {
-      const int64_t item = (int64_t)(cub[s] + i) * heads + h;
-      const float2 ml = __ldg(reinterpret_cast<const float2*>(part_ml + item * 2 * G) + j);
-      const float wgt = ex2(ml.x - mx);
-      L += ml.y * wgt;
-      const float* po = part_o + (item * G + j) * HD + lane * EPL;
-#pragma unroll
-      for (int e = 0; e < EPL; e += 2) {
-        const float2 v = __ldg(reinterpret_cast<const float2*>(po + e));
-        acc[e] += wgt * v.x;
-        acc[e + 1] += wgt * v.y;
-      }
-    }
-    const float inv = n ? 1.0f / L : 0.0f;
-    uint32_t wv[EPL / 2];
-#pragma unroll
-    for (int e = 0; e < EPL; e += 2) wv[e / 2] = pack2<DT>(acc[e] * inv, acc[e + 1] * inv);
-    uint8_t* dst = out + ((int64_t)s * qheads + qh) * HD * 2 + lane * EPL * 2;
-    if (EPL == 4) *reinterpret_cast<uint2*>(dst) = make_uint2(wv[0], wv[1]);
-    else *reinterpret_cast<uint32_t*>(dst) = wv[0];
+    if (n < 2) continue;
+    combine_splits<DT, HD>(part_o, part_ml, out, s, qh / G, qh % G, G, heads, cub[s], n, lane);
   }
 }
 
@@ -359,9 +449,19 @@ namespace {
 // a (max, sum) pair per query head, all f32.
 size_t split_bytes(int heads, int G, int hd) { return (size_t)heads * G * (hd + 2) * sizeof(float); }
 
-using AttnFn = void (*)(PoolGeo, int, const uint8_t*, int, const int32_t*, int, const int32_t*, int, float, float*,
-                        float*, int64_t, int32_t*);
-using CombineFn = void (*)(const int32_t*, int, int, int, const float*, const float*, uint8_t*, int64_t);
+using AttnFn = void (*)(PoolGeo, int, const uint8_t*, int, const int32_t*, int, const int32_t*, int, int, float,
+                        float*, float*, int64_t, uint8_t*, int32_t*);
+using CombineFn = void (*)(const int32_t*, int, int, int, int, const float*, const float*, uint8_t*, int64_t);
+
+// The configuration the dispatch uses: stages in flight per warp, CTAs per
+// SM, queries in shared memory.
+constexpr int ATT_STAGES = 2, ATT_MINB = 3;
+constexpr bool ATT_QSMEM = true;
+
+size_t attn_smem(int nseq, int hd, int stages, bool qsmem) {
+  const size_t scan_bytes = ((size_t)2 * (nseq + 1) * 4 + 127) & ~(size_t)127;
+  return scan_bytes + (size_t)ATT_WARPS * ((size_t)stages * 2 * ATT_CHUNK * hd * 2 + (qsmem ? ATT_CHUNK * hd * 2 : 0));
+}
 
 }  // namespace
 
@@ -406,26 +506,28 @@ rmlx_status rmlx_kv_decode_attention(rmlx_kv_pool* p, int32_t layer, const void*
   DeviceGuard dg(p->device);
   cudaStream_t st = (cudaStream_t)stream;
   const bool bf = c.dtype == RMLX_BF16;
-  AttnFn fa = hd == 128 ? (bf ? paged_decode_attn_kernel<RMLX_BF16, 128> : paged_decode_attn_kernel<RMLX_F16, 128>)
-                        : (bf ? paged_decode_attn_kernel<RMLX_BF16, 64> : paged_decode_attn_kernel<RMLX_F16, 64>);
+  AttnFn fa = hd == 128 ? (bf ? paged_decode_attn_kernel<RMLX_BF16, 128, ATT_STAGES, ATT_MINB, ATT_QSMEM>
+                              : paged_decode_attn_kernel<RMLX_F16, 128, ATT_STAGES, ATT_MINB, ATT_QSMEM>)
+                        : (bf ? paged_decode_attn_kernel<RMLX_BF16, 64, ATT_STAGES, ATT_MINB, ATT_QSMEM>
+                              : paged_decode_attn_kernel<RMLX_F16, 64, ATT_STAGES, ATT_MINB, ATT_QSMEM>);
   CombineFn fc = hd == 128 ? (bf ? attn_combine_kernel<RMLX_BF16, 128> : attn_combine_kernel<RMLX_F16, 128>)
                            : (bf ? attn_combine_kernel<RMLX_BF16, 64> : attn_combine_kernel<RMLX_F16, 64>);
-  const size_t scan_bytes = ((size_t)2 * (num_seqs + 1) * 4 + 127) & ~(size_t)127;
-  const size_t smem = scan_bytes + (size_t)ATT_WARPS * ATT_STAGES * 2 * ATT_CHUNK * hd * 2;
+  const size_t smem = attn_smem(num_seqs, hd, ATT_STAGES, ATT_QSMEM);
   rmlx_status s;
   if ((s = prepare_smem(fa, smem)) != RMLX_OK) return s;
   const int grid = persistent_grid(fa, ATT_WARPS * 32, smem, p->num_sms);
   const float scale_log2 = softmax_scale * 1.4426950408889634f;  // log2(e)
   cudaError_t e = launch_pdl(fa, dim3(grid), dim3(ATT_WARPS * 32), smem, st, p->geo(), (int)layer,
                              static_cast<const uint8_t*>(q), G, block_tables, (int)block_table_stride, seq_lens,
-                             (int)num_seqs, scale_log2, part_o, part_ml, cap, p->err);
+                             (int)num_seqs, ATT_SPLIT, scale_log2, part_o, part_ml, cap, static_cast<uint8_t*>(out),
+                             p->err);
   if (e != cudaSuccess) return cuda_check(e, "decode attention launch");
   const size_t csmem = (size_t)2 * (num_seqs + 1) * 4;
   if ((s = prepare_smem(fc, csmem)) != RMLX_OK) return s;
   const int64_t warps = (int64_t)num_seqs * heads * G;
   const int cgrid = (int)std::min<int64_t>((warps + 7) / 8, (int64_t)p->num_sms * 8);
-  e = launch_pdl(fc, dim3(cgrid), dim3(256), csmem, st, seq_lens, (int)num_seqs, heads, G, part_o, part_ml,
-                 static_cast<uint8_t*>(out), cap);
+  e = launch_pdl(fc, dim3(cgrid), dim3(256), csmem, st, seq_lens, (int)num_seqs, ATT_SPLIT, heads, G, part_o,
+                 part_ml, static_cast<uint8_t*>(out), cap);
   if (e != cudaSuccess) return cuda_check(e, "attention combine launch");
   return cuda_check(cudaGetLastError(), "decode attention launch");
 }
