@@ -110,6 +110,12 @@ WORKLOADS = {
         "decode step with attention reading the pool in place: 32 layers x 8 KV heads x 128, block 16, bf16, "
         "32 query heads (4 per KV head), batch 64, ctx U[512,4096]; append 1 token/seq/layer, then paged decode "
         "attention of every layer (no gathered copy)", seed=0x5EED + 2, attn_g=4),
+    "attn8": Workload(
+        "attn8", "KV quant-append + paged decode attention over 8-bit codes HBM GB/s (decode step, Llama-3.1-8B shape)",
+        "decode step with attention reading an 8-bit pool in place: 32 layers x 8 KV heads x 128, block 16, 8-bit "
+        "codes, group 64, fp16 scale/zero, 32 query heads (4 per KV head), batch 64, ctx U[512,4096]; quantise-on-"
+        "append 1 token/seq/layer, then paged decode attention of every layer (codes dequantised in shared memory)",
+        seed=0x5EED + 2, attn_g=4, bits=8),
 }
 
 

@@ -340,11 +340,15 @@ RMLX_API rmlx_status rmlx_kv_gather(rmlx_kv_pool* p, int32_t layer, const int32_
  * over the seq_lens[s] rows that rmlx_kv_gather would return for (s, layer).
  * q and out are [num_seqs][num_kv_heads * q_heads_per_kv][head_dim] in the
  * pool's type; f32 scores and sums; a sequence of length 0 gives zeros.
- * F16/BF16 pools with head_dim 64 or 128, q_heads_per_kv in [1, 16].
+ * F16/BF16 pools with head_dim 64 or 128, q_heads_per_kv in [1, 16]; a
+ * quantised pool (4 or 8 bits) is read as its codes and dequantised in the
+ * kernel to the same rows rmlx_kv_gather returns for it.
  * workspace: at least rmlx_kv_attention_workspace_size(...) bytes for a
  * launch whose seq_lens sum to at most max_total_tokens; a launch that needs
  * more is flagged in the pool's device error word (rmlx_kv_pool_check bit 4)
- * and leaves out unwritten. */
+ * and leaves out unwritten.  Launches on one pool hand out work through a
+ * counter the pool owns: order them on one stream (or otherwise one after
+ * another), not concurrently. */
 RMLX_API rmlx_status rmlx_kv_attention_workspace_size(const rmlx_kv_pool* p, int32_t q_heads_per_kv, int32_t num_seqs,
                                                       int64_t max_total_tokens, size_t* bytes);
 RMLX_API rmlx_status rmlx_kv_decode_attention(rmlx_kv_pool* p, int32_t layer, const void* q, int32_t q_heads_per_kv,

@@ -28,6 +28,7 @@
 
 #include <algorithm>
 
+#include "dequant.cuh"
 #include "kv_pool_internal.cuh"
 
 namespace rmlx {
@@ -73,7 +74,27 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t&
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, int src_bytes) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
 }
+// 4- and 8-byte async copies (short scale/zero rows), same zero-fill rule.
+__device__ __forceinline__ void cp_async8(uint32_t dst, const void* src, int src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src, int src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ void sts128(uint32_t a, uint4 v) {
+  asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w) : "memory");
+}
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
@@ -162,27 +183,38 @@ __device__ __forceinline__ void combine_splits(const float* part_o, const float*
 // queries in shared memory (same layout, 16 rows) and reads their A
 // fragments with ldmatrix at every step instead of holding them in
 // registers.  `split` tokens per work item (a multiple of 16).
-template <int DT, int HD, int STAGES, int MINB, bool QSMEM>
+//
+// BITS = 4 or 8: a quantised pool.  A stage then holds the chunk's raw K
+// code rows, K scale/zero rows, V code rows and V scale/zero rows as they
+// lie in the tiles; after the wait the warp dequantises them (dq_pair, the
+// same values the dequantising gather produces, rounded to the pool's type)
+// into one swizzled K/V tile in the layout above, writing zeros for rows
+// past the sequence's end, and the tensor-core steps read that tile.
+template <int DT, int HD, int STAGES, int MINB, bool QSMEM, int BITS = 0, bool MF32 = false>
 __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
     paged_decode_attn_kernel(PoolGeo g, int layer, const uint8_t* __restrict__ q, int G,
                              const int32_t* __restrict__ bt, int bt_stride, const int32_t* __restrict__ lens,
                              int nseq, int split, float scale_log2, float* __restrict__ part_o,
                              float* __restrict__ part_ml, int64_t cap_splits, uint8_t* __restrict__ out,
-                             int32_t* err) {
-  constexpr int ROWB = HD * 2;  // bytes of one K or V row
+                             int gs_log2, unsigned long long* __restrict__ work, int32_t* err) {
+  constexpr int ROWB = HD * 2;  // bytes of one K or V row (of the pool's type)
   constexpr int CPR = ROWB / 16;
   constexpr int KT = HD / 16;  // k-steps of S = Q K^T
   constexpr int NT = HD / 8;   // n-tiles of O
-  constexpr int STAGE = 2 * ATT_CHUNK * ROWB;
   constexpr unsigned FULL = 0xffffffffu;
+  // stage layout: plain, K then V rows; quantised, K codes | K meta | V codes | V meta
+  const int RB = g.row_bytes, MB = g.meta_row_bytes;        // code / meta row bytes
+  const int RAWH = ATT_CHUNK * (RB + MB);                   // one of K, V in a quantised stage
+  const int STAGE = BITS ? 2 * RAWH : 2 * ATT_CHUNK * ROWB;  // bytes per stage
   extern __shared__ __align__(128) uint8_t smem[];
   int32_t* cub = reinterpret_cast<int32_t*>(smem);
   int32_t* cut = cub + nseq + 1;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const size_t scan_bytes = ((size_t)2 * (nseq + 1) * 4 + 127) & ~(size_t)127;
-  constexpr int WBYTES = STAGES * STAGE + (QSMEM ? ATT_CHUNK * ROWB : 0);  // per warp
+  const int WBYTES = STAGES * STAGE + (BITS ? 2 * ATT_CHUNK * ROWB : 0) + (QSMEM ? ATT_CHUNK * ROWB : 0);
   const uint32_t wbuf = (uint32_t)__cvta_generic_to_shared(smem + scan_bytes) + warp * WBYTES;
-  const uint32_t qbuf = wbuf + STAGES * STAGE;
+  const uint32_t tbuf = wbuf + STAGES * STAGE;                          // dequantised K/V tile
+  const uint32_t qbuf = tbuf + (BITS ? 2 * ATT_CHUNK * ROWB : 0);
   pdl_wait();
   pdl_release();
   scan_seq_lens(lens, nseq, split, cub, cut);
@@ -202,9 +234,15 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
   const int r = lane >> 2, c = lane & 3;
   const int64_t vdelta = (int64_t)g.heads * g.tile_bytes;  // V tile of (block, layer, head) after its K tile
   const bool aligned_blocks = (g.bs % ATT_CHUNK) == 0;     // a chunk never crosses a block
-  const int64_t nwarps = (int64_t)gridDim.x * ATT_WARPS;
-
-  for (int64_t it = (int64_t)blockIdx.x * ATT_WARPS + warp; it < items; it += nwarps) {
+  // work items are handed out in order by a counter (zero at launch; the
+  // combine kernel puts it back to zero), so warps that finish early take
+  // the remaining items
+  auto next_item = [&]() -> int64_t {
+    unsigned long long v = 0;
+    if (lane == 0) v = atomicAdd(work, 1ULL);
+    return (int64_t)__shfl_sync(FULL, v, 0);
+  };
+  for (int64_t it = next_item(); it < items; it = next_item()) {
     const int h = (int)(it % g.heads);
     const int64_t sg = it / g.heads;
     const int s = find_seq(cub, nseq, sg);
@@ -242,6 +280,76 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
     auto load_chunk = [&](int ci) {
       const uint32_t dst = wbuf + (ci % STAGES) * STAGE;
       const int tc = t_begin + ci * ATT_CHUNK;
+      if (BITS) {
+        if (aligned_blocks) {
+          // 16 code rows and 16 meta rows, each a contiguous run of the tile
+          const int32_t blk = __ldg(btrow + tc / g.bs);
+          const bool ok = blk >= 0 && blk < g.nblocks;
+          if (!ok && lane == 0) atomicOr(err, DEV_ERR_BLOCK);
+          const int n = ok ? 16 : 0;
+          const uint8_t* tile = ok ? g.base + g.tile_off(blk, layer, 0, h) : g.base;
+          const int r0 = tc % g.bs;
+          const uint8_t* codes = tile + (int64_t)r0 * RB;
+          const uint8_t* meta = tile + (int64_t)g.bs * RB + (int64_t)r0 * MB;
+          const int cc = ATT_CHUNK * RB / 16, mc = ATT_CHUNK * MB / 16;
+          for (int x = lane; x < cc + mc; x += 32) {
+            const bool isc = x < cc;
+            const int off = (isc ? x : x - cc) * 16;
+            const uint8_t* sp = n ? (isc ? codes : meta) + off : g.base;
+            const uint32_t so = (isc ? 0 : ATT_CHUNK * RB) + off;
+            cp_async16(dst + so, sp, n);
+            cp_async16(dst + RAWH + so, n ? sp + vdelta : g.base, n);
+          }
+        } else {
+          // rows from different blocks: one row's codes and meta at a time
+          const int t = tc + (lane & 15);
+          const uint8_t* tile = g.base;
+          int nb = 0;
+          if (t < t_end) {
+            const int32_t blk = __ldg(btrow + t / g.bs);
+            if (blk >= 0 && blk < g.nblocks) {
+              tile = g.base + g.tile_off(blk, layer, 0, h);
+              nb = 1;
+            } else if (lane < 16) {
+              atomicOr(err, DEV_ERR_BLOCK);
+            }
+          }
+          const int rw = t % g.bs;
+          const unsigned long long cp_ = reinterpret_cast<unsigned long long>(tile + (int64_t)rw * RB);
+          const unsigned long long mp_ = reinterpret_cast<unsigned long long>(tile + (int64_t)g.bs * RB + (int64_t)rw * MB);
+          const int cpr = RB / 16, mcs = MB < 16 ? MB : 16, mpr = MB / mcs;
+          // each row's pointers by shuffle (all lanes), then its copies
+          for (int row = 0; row < ATT_CHUNK; ++row) {
+            const int ok = __shfl_sync(FULL, nb, row);
+            const uint8_t* rc = reinterpret_cast<const uint8_t*>(__shfl_sync(FULL, cp_, row));
+            const uint8_t* rm = reinterpret_cast<const uint8_t*>(__shfl_sync(FULL, mp_, row));
+            for (int k = lane; k < cpr + mpr; k += 32) {
+              if (k < cpr) {
+                const uint32_t so = row * RB + k * 16;
+                cp_async16(dst + so, ok ? rc + k * 16 : g.base, ok ? 16 : 0);
+                cp_async16(dst + RAWH + so, ok ? rc + vdelta + k * 16 : g.base, ok ? 16 : 0);
+              } else {
+                const int m = k - cpr;
+                const uint32_t so = ATT_CHUNK * RB + row * MB + m * mcs;
+                const uint8_t* a = ok ? rm + m * mcs : g.base;
+                const uint8_t* b = ok ? rm + vdelta + m * mcs : g.base;
+                if (mcs == 16) {
+                  cp_async16(dst + so, a, ok ? 16 : 0);
+                  cp_async16(dst + RAWH + so, b, ok ? 16 : 0);
+                } else if (mcs == 8) {
+                  cp_async8(dst + so, a, ok ? 8 : 0);
+                  cp_async8(dst + RAWH + so, b, ok ? 8 : 0);
+                } else {
+                  cp_async4(dst + so, a, ok ? 4 : 0);
+                  cp_async4(dst + RAWH + so, b, ok ? 4 : 0);
+                }
+              }
+            }
+          }
+        }
+        cp_async_commit();
+        return;
+      }
       if (aligned_blocks) {
         // the chunk's 16 rows are contiguous in one K tile (and one V tile)
         const int32_t blk = __ldg(btrow + tc / g.bs);
@@ -300,8 +408,50 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
       else cp_async_commit();
       cp_async_wait<STAGES - 1>();
       __syncwarp();
-      const uint32_t kb = wbuf + (ci % STAGES) * STAGE, vb = kb + ATT_CHUNK * ROWB;
+      const uint32_t sb = wbuf + (ci % STAGES) * STAGE;
+      uint32_t kb = sb, vb = sb + ATT_CHUNK * ROWB;
       const int tc = t_begin + ci * ATT_CHUNK;
+      if (BITS) {
+        // dequantise the stage into the K/V tile; rows past the end are zeros
+        constexpr int GPR = HD / 8;  // 16-byte groups of 8 elements per row
+        const int nval = min(ATT_CHUNK, t_end - tc);
+        for (int x = lane; x < 2 * ATT_CHUNK * GPR; x += 32) {
+          const int kv = x / (ATT_CHUNK * GPR), rem = x - kv * (ATT_CHUNK * GPR);
+          const int row = rem / GPR, g8 = rem - row * GPR;
+          uint4 w4 = make_uint4(0u, 0u, 0u, 0u);
+          if (row < nval) {
+            const uint32_t raw = sb + kv * RAWH;
+            uint2 cw = make_uint2(0u, 0u);
+            if (BITS == 8) cw = lds64(raw + row * RB + g8 * 8);
+            else cw.x = lds32(raw + row * RB + g8 * 4);
+            const uint32_t ma = raw + ATT_CHUNK * RB + row * MB + ((g8 * 8) >> gs_log2) * (MF32 ? 8 : 4);
+            float sc, zr;
+            if (MF32) {
+              const uint2 m = lds64(ma);
+              sc = __uint_as_float(m.x);
+              zr = __uint_as_float(m.y);
+            } else {
+              const uint32_t m = lds32(ma);
+              const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&m));
+              sc = f.x;
+              zr = f.y;
+            }
+            uint32_t lo4 = 0, hi4 = 0;
+            if (BITS == 4) {
+              lo4 = cw.x & 0x0F0F0F0Fu;
+              hi4 = (cw.x >> 4) & 0x0F0F0F0Fu;
+            }
+            float f[8];
+#pragma unroll
+            for (int e = 0; e < 8; e += 2) dq_pair<BITS == 4 ? 4 : 8, MF32>(cw, lo4, hi4, e, sc, zr, f[e], f[e + 1]);
+            w4 = make_uint4(pack2<DT>(f[0], f[1]), pack2<DT>(f[2], f[3]), pack2<DT>(f[4], f[5]), pack2<DT>(f[6], f[7]));
+          }
+          sts128(tbuf + kv * ATT_CHUNK * ROWB + row * ROWB + ((g8 ^ (row & 7)) << 4), w4);
+        }
+        __syncwarp();
+        kb = tbuf;
+        vb = tbuf + ATT_CHUNK * ROWB;
+      }
 
       // S = Q K^T: two n-tiles of 8 tokens
       float sacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
@@ -417,7 +567,7 @@ template <int DT, int HD>
 __global__ void __launch_bounds__(256) attn_combine_kernel(const int32_t* __restrict__ lens, int nseq, int split,
                                                            int heads, int G, const float* __restrict__ part_o,
                                                            const float* __restrict__ part_ml, uint8_t* __restrict__ out,
-                                                           int64_t cap_splits) {
+                                                           int64_t cap_splits, unsigned long long* __restrict__ work) {
   extern __shared__ int32_t cs[];
   int32_t* cub = cs;
   int32_t* cut = cs + nseq + 1;
@@ -426,6 +576,7 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const int32_t* __rest
   pdl_release();
   scan_seq_lens(lens, nseq, split, cub, cut);
   pdl_wait();
+  if (blockIdx.x == 0 && threadIdx.x == 0) *work = 0;  // the split kernel has taken all its items
   if (cub[nseq] > cap_splits) return;  // flagged by the split kernel
   const int lane = threadIdx.x & 31;
   const int qheads = heads * G;
@@ -450,17 +601,33 @@ namespace {
 size_t split_bytes(int heads, int G, int hd) { return (size_t)heads * G * (hd + 2) * sizeof(float); }
 
 using AttnFn = void (*)(PoolGeo, int, const uint8_t*, int, const int32_t*, int, const int32_t*, int, int, float,
-                        float*, float*, int64_t, uint8_t*, int32_t*);
-using CombineFn = void (*)(const int32_t*, int, int, int, int, const float*, const float*, uint8_t*, int64_t);
+                        float*, float*, int64_t, uint8_t*, int, unsigned long long*, int32_t*);
+using CombineFn = void (*)(const int32_t*, int, int, int, int, const float*, const float*, uint8_t*, int64_t,
+                           unsigned long long*);
 
 // The configuration the dispatch uses: stages in flight per warp, CTAs per
 // SM, queries in shared memory.
 constexpr int ATT_STAGES = 2, ATT_MINB = 3;
 constexpr bool ATT_QSMEM = true;
 
-size_t attn_smem(int nseq, int hd, int stages, bool qsmem) {
+// Dynamic shared memory of one CTA: the scan arrays, then per warp its
+// stages (raw code and meta rows for a quantised pool), the dequantised K/V
+// tile (quantised pools) and the queries (qsmem).
+size_t attn_smem(int nseq, int hd, int stages, bool qsmem, int bits, int row_bytes, int meta_row_bytes) {
   const size_t scan_bytes = ((size_t)2 * (nseq + 1) * 4 + 127) & ~(size_t)127;
-  return scan_bytes + (size_t)ATT_WARPS * ((size_t)stages * 2 * ATT_CHUNK * hd * 2 + (qsmem ? ATT_CHUNK * hd * 2 : 0));
+  const size_t rowb = (size_t)hd * 2;
+  const size_t stage = bits ? 2 * ATT_CHUNK * (size_t)(row_bytes + meta_row_bytes) : 2 * ATT_CHUNK * rowb;
+  return scan_bytes + (size_t)ATT_WARPS * (stages * stage + (bits ? 2 * ATT_CHUNK * rowb : 0) +
+                                           (qsmem ? ATT_CHUNK * rowb : 0));
+}
+
+template <int DT, int HD>
+AttnFn pick_attn(int bits, bool mf32) {
+  if (bits == 8) return mf32 ? paged_decode_attn_kernel<DT, HD, ATT_STAGES, ATT_MINB, ATT_QSMEM, 8, true>
+                             : paged_decode_attn_kernel<DT, HD, ATT_STAGES, ATT_MINB, ATT_QSMEM, 8, false>;
+  if (bits == 4) return mf32 ? paged_decode_attn_kernel<DT, HD, ATT_STAGES, ATT_MINB, ATT_QSMEM, 4, true>
+                             : paged_decode_attn_kernel<DT, HD, ATT_STAGES, ATT_MINB, ATT_QSMEM, 4, false>;
+  return paged_decode_attn_kernel<DT, HD, ATT_STAGES, ATT_MINB, ATT_QSMEM>;
 }
 
 }  // namespace
@@ -483,7 +650,6 @@ rmlx_status rmlx_kv_decode_attention(rmlx_kv_pool* p, int32_t layer, const void*
                                      size_t workspace_bytes, void* stream) {
   if (!p) return fail(RMLX_E_BAD_ARG, "NULL pool");
   const rmlx_pool_config& c = p->cfg;
-  if (c.quant_bits != 0) return fail(RMLX_E_BAD_ARG, "decode attention reads f16/bf16 pools, not quantised ones");
   if (c.dtype != RMLX_F16 && c.dtype != RMLX_BF16) return fail(RMLX_E_BAD_ARG, "decode attention needs an F16 or BF16 pool");
   if (c.head_dim != 64 && c.head_dim != 128) return fail(RMLX_E_BAD_ARG, "decode attention supports head_dim 64 or 128");
   if (q_heads_per_kv < 1 || q_heads_per_kv > 16) return fail(RMLX_E_BAD_ARG, "q_heads_per_kv must be in [1, 16]");
@@ -506,13 +672,22 @@ rmlx_status rmlx_kv_decode_attention(rmlx_kv_pool* p, int32_t layer, const void*
   DeviceGuard dg(p->device);
   cudaStream_t st = (cudaStream_t)stream;
   const bool bf = c.dtype == RMLX_BF16;
-  AttnFn fa = hd == 128 ? (bf ? paged_decode_attn_kernel<RMLX_BF16, 128, ATT_STAGES, ATT_MINB, ATT_QSMEM>
-                              : paged_decode_attn_kernel<RMLX_F16, 128, ATT_STAGES, ATT_MINB, ATT_QSMEM>)
-                        : (bf ? paged_decode_attn_kernel<RMLX_BF16, 64, ATT_STAGES, ATT_MINB, ATT_QSMEM>
-                              : paged_decode_attn_kernel<RMLX_F16, 64, ATT_STAGES, ATT_MINB, ATT_QSMEM>);
+  const int bits = c.quant_bits;
+  const bool mf32 = c.meta_dtype == RMLX_F32;
+  AttnFn fa = hd == 128 ? (bf ? pick_attn<RMLX_BF16, 128>(bits, mf32) : pick_attn<RMLX_F16, 128>(bits, mf32))
+                        : (bf ? pick_attn<RMLX_BF16, 64>(bits, mf32) : pick_attn<RMLX_F16, 64>(bits, mf32));
   CombineFn fc = hd == 128 ? (bf ? attn_combine_kernel<RMLX_BF16, 128> : attn_combine_kernel<RMLX_F16, 128>)
                            : (bf ? attn_combine_kernel<RMLX_BF16, 64> : attn_combine_kernel<RMLX_F16, 64>);
-  const size_t smem = attn_smem(num_seqs, hd, ATT_STAGES, ATT_QSMEM);
+  if (!p->attn_work) {  // the item counter: pool memory, zero between launches
+    void* w = nullptr;
+    if (cudaMalloc(&w, 16) != cudaSuccess || cudaMemset(w, 0, 16) != cudaSuccess) {
+      if (w) cudaFree(w);
+      return cuda_check(cudaGetLastError(), "attention item counter");
+    }
+    p->attn_work = static_cast<unsigned long long*>(w);
+  }
+  const size_t smem = attn_smem(num_seqs, hd, ATT_STAGES, ATT_QSMEM, bits, (int)p->row_bytes, (int)p->meta_row_bytes);
+  if (smem > 227 * 1024) return fail(RMLX_E_BAD_ARG, "num_seqs too large for one decode attention launch");
   rmlx_status s;
   if ((s = prepare_smem(fa, smem)) != RMLX_OK) return s;
   const int grid = persistent_grid(fa, ATT_WARPS * 32, smem, p->num_sms);
@@ -520,15 +695,18 @@ rmlx_status rmlx_kv_decode_attention(rmlx_kv_pool* p, int32_t layer, const void*
   cudaError_t e = launch_pdl(fa, dim3(grid), dim3(ATT_WARPS * 32), smem, st, p->geo(), (int)layer,
                              static_cast<const uint8_t*>(q), G, block_tables, (int)block_table_stride, seq_lens,
                              (int)num_seqs, ATT_SPLIT, scale_log2, part_o, part_ml, cap, static_cast<uint8_t*>(out),
-                             p->err);
+                             bits ? log2i(c.group_size) : 0, p->attn_work, p->err);
   if (e != cudaSuccess) return cuda_check(e, "decode attention launch");
   const size_t csmem = (size_t)2 * (num_seqs + 1) * 4;
   if ((s = prepare_smem(fc, csmem)) != RMLX_OK) return s;
   const int64_t warps = (int64_t)num_seqs * heads * G;
   const int cgrid = (int)std::min<int64_t>((warps + 7) / 8, (int64_t)p->num_sms * 8);
   e = launch_pdl(fc, dim3(cgrid), dim3(256), csmem, st, seq_lens, (int)num_seqs, ATT_SPLIT, heads, G, part_o,
-                 part_ml, static_cast<uint8_t*>(out), cap);
-  if (e != cudaSuccess) return cuda_check(e, "attention combine launch");
+                 part_ml, static_cast<uint8_t*>(out), cap, p->attn_work);
+  if (e != cudaSuccess) {
+    cudaMemsetAsync(p->attn_work, 0, 16, st);  // the combine would have reset the counter
+    return cuda_check(e, "attention combine launch");
+  }
   return cuda_check(cudaGetLastError(), "decode attention launch");
 }
 

@@ -98,6 +98,8 @@ struct rmlx_kv_pool {
   // shared-memory size used (the kernel is fixed by the pool's config).
   size_t gather_smem = 0;
   int gather_grid = 0;
+  // Work-item counter of the decode attention (zero between launches).
+  unsigned long long* attn_work = nullptr;
   rmlx::PoolGeo geo() const {
     rmlx::PoolGeo g;
     g.base = base;

@@ -149,14 +149,69 @@ def test_bad_block_id_flagged(cuda):
     pool.close()
 
 
+def run_attn_quant(cuda, L, H, D, bs, N, dt, G, lens, seed, bits, gs, meta, layer=0):
+    """Quantised pool filled through the quantise-on-append path; the
+    reference reads the rows the dequantising gather returns."""
+    import torch
+    from helpers import rand_rows, slots_for
+    rng = np.random.default_rng(seed)
+    pool = rmlx_kv.KVPool(L, H, D, bs, N, dtype=dt, quant_bits=bits, group_size=gs, meta_dtype=meta)
+    pool.write(np.zeros(pool.layout.bytes, np.uint8))
+    lens = np.array(lens, dtype=np.int64)
+    bt, _ = block_tables(rng, lens, bs, N)
+    pos = [(s, p) for s in range(len(lens)) for p in range(int(lens[s]))]
+    if pos:
+        T = len(pos)
+        k = rand_rows(rng, (L, T, H, D), dt)  # N(0,1): the tolerance above assumes |V| <~ 4.5
+        v = rand_rows(rng, (L, T, H, D), dt)
+        pool.append(to_dev(k), to_dev(v), to_dev(slots_for(bt, bs, pos)), T)
+    q = orc.f32_to_dtype(rng.standard_normal((len(lens), H * G, D), dtype=np.float32), dt)
+    scale = 1.0 / np.sqrt(D)
+    ws = torch.empty(max(pool.attention_workspace_size(G, len(lens), int(lens.sum())), 16), dtype=torch.uint8,
+                     device=cuda)
+    out = torch.full((len(lens), H * G, D), -7, dtype=torch.int16, device=cuda)
+    pool.decode_attention(layer, to_dev(q), G, to_dev(bt), bt.shape[1], to_dev(lens.astype(np.int32)), len(lens),
+                          scale, out, ws)
+    torch.cuda.synchronize()
+    assert pool.check() == 0
+    got = orc.dtype_to_f32(out.cpu().numpy().view(np.uint16), dt).astype(np.float64)
+    want = _reference(pool, layer, q, G, bt, lens, scale, dt, cuda)
+    err = np.abs(got - want)
+    mx, rms = TOL[dt]
+    assert np.isfinite(got).all()
+    assert err.max() <= mx, f"max abs error {err.max()}"
+    assert np.sqrt((err ** 2).mean()) <= rms
+    assert (got[lens == 0] == 0).all()
+    pool.close()
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+@pytest.mark.parametrize("meta", [orc.F16, orc.F32])
+def test_quantised_pool(cuda, bits, meta):
+    """8 KV heads x 128, group 64, 4 query heads per KV head; K/V rows as
+    the dequantising gather returns them (codes read in place)."""
+    run_attn_quant(cuda, 2, 8, 128, 16, 256, orc.BF16, 4, [38, 129, 256, 513, 0, 1000], 70 + bits, bits, 64, meta,
+                   layer=1)
+
+
+@pytest.mark.parametrize("bs,D,gs,dt", [(8, 128, 32, orc.BF16), (1, 64, 16, orc.F16), (32, 64, 64, orc.F16),
+                                        (5, 128, 128, orc.BF16)])
+def test_quantised_block_sizes_and_groups(cuda, bs, D, gs, dt):
+    """bs 8, 1 and 5: chunks span blocks (row-by-row copies of codes and of
+    4-, 8- or 16-byte scale/zero rows); 32: two chunks per block."""
+    N = 700 // bs + 40
+    for bits in (8, 4):
+        run_attn_quant(cuda, 1, 2, D, bs, N, dt, 8, [3, 16, 31, 300], 80 + bs + bits, bits, gs, orc.F16)
+
+
 def test_bad_arguments(cuda):
     import torch
     q = torch.zeros(4096, dtype=torch.bfloat16, device=cuda)
     ws = torch.empty(1 << 20, dtype=torch.uint8, device=cuda)
     bt = to_dev(np.zeros((1, 1), np.int32))
     ln = to_dev(np.array([1], np.int32))
-    quant = rmlx_kv.KVPool(1, 1, 128, 16, 4, dtype=orc.BF16, quant_bits=8, group_size=64)
-    with pytest.raises(rmlx_kv.RmlxError, match="quantised"):
+    quant = rmlx_kv.KVPool(1, 1, 256, 16, 4, dtype=orc.BF16, quant_bits=8, group_size=64)
+    with pytest.raises(rmlx_kv.RmlxError, match="head_dim"):
         quant.decode_attention(0, q, 1, bt, 1, ln, 1, 0.1, q, ws)
     p256 = rmlx_kv.KVPool(1, 1, 256, 16, 4, dtype=orc.BF16)
     with pytest.raises(rmlx_kv.RmlxError, match="head_dim"):
