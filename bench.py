@@ -679,6 +679,8 @@ def main():
     ap.add_argument("--bits", type=int, default=0, choices=[0, 8],
                     help="llama70b workload: 0 = bf16 pool, 8 = 8-bit codes")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kv-heads", type=int, default=None,
+                    help="override the workload's KV heads (e.g. 1: one GPU's shard of an 8-GPU run)")
     ap.add_argument("--layers", type=int, default=None,
                     help="layers in the pool (profiling runs only; a gather moves the same bytes per layer)")
     ap.add_argument("--quick", action="store_true", help="device-timed loop only (profiling runs)")
@@ -717,6 +719,8 @@ def main():
     w = WORKLOADS[args.workload]
     if args.layers:
         w.layers = args.layers
+    if args.kv_heads:
+        w.heads = args.kv_heads
 
     rank, world, local = env_int("RANK", 0), env_int("WORLD_SIZE", 1), env_int("LOCAL_RANK", 0)
     if args.impl == "reference":

@@ -92,6 +92,11 @@ __device__ __forceinline__ uint2 lds64(uint32_t a) {
   asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a) : "memory");
   return v;
 }
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a) : "memory");
+  return v;
+}
 __device__ __forceinline__ void sts128(uint32_t a, uint4 v) {
   asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w) : "memory");
 }
@@ -176,6 +181,22 @@ __device__ __forceinline__ void combine_splits(const float* part_o, const float*
   else *reinterpret_cast<uint32_t*>(dst) = wv[0];
 }
 
+// Split size of a launch: 256 tokens, halved (down to 64) while the launch
+// would have fewer than `target` work items and twice its splits still fit
+// the workspace (cap splits); leaves the scan of the chosen size in cub/cut.
+// Every CTA of both kernels runs it on the same inputs, so they agree.
+__device__ __forceinline__ int pick_split(const int32_t* lens, int nseq, int heads, int64_t target, int64_t cap,
+                                          int32_t* cub, int32_t* cut) {
+  int split = ATT_SPLIT;
+  scan_seq_lens(lens, nseq, split, cub, cut);
+  while (split > 64 && (int64_t)cub[nseq] * heads < target && 2 * (int64_t)cub[nseq] <= cap) {
+    split >>= 1;
+    __syncthreads();  // everyone has read cub before it is rewritten
+    scan_seq_lens(lens, nseq, split, cub, cut);
+  }
+  return split;
+}
+
 // Shared-memory layout of one stage: K rows then V rows of a 16-token chunk,
 // row-major, 16-byte column chunk c of row r stored at slot c ^ (r & 7) so
 // that the 8 row addresses of every ldmatrix hit 8 different bank groups.
@@ -186,15 +207,16 @@ __device__ __forceinline__ void combine_splits(const float* part_o, const float*
 //
 // BITS = 4 or 8: a quantised pool.  A stage then holds the chunk's raw K
 // code rows, K scale/zero rows, V code rows and V scale/zero rows as they
-// lie in the tiles; after the wait the warp dequantises them (dq_pair, the
-// same values the dequantising gather produces, rounded to the pool's type)
-// into one swizzled K/V tile in the layout above, writing zeros for rows
-// past the sequence's end, and the tensor-core steps read that tile.
+// lie in the tiles; after the wait the warp dequantises K (dq_pair, the same
+// values the dequantising gather produces, rounded to the pool's type) into
+// one swizzled tile in the layout above, writing zeros for rows past the
+// sequence's end, computes S from it, and then dequantises V into the same
+// tile for O += P V.
 template <int DT, int HD, int STAGES, int MINB, bool QSMEM, int BITS = 0, bool MF32 = false>
 __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
     paged_decode_attn_kernel(PoolGeo g, int layer, const uint8_t* __restrict__ q, int G,
                              const int32_t* __restrict__ bt, int bt_stride, const int32_t* __restrict__ lens,
-                             int nseq, int split, float scale_log2, float* __restrict__ part_o,
+                             int nseq, int64_t target, float scale_log2, float* __restrict__ part_o,
                              float* __restrict__ part_ml, int64_t cap_splits, uint8_t* __restrict__ out,
                              int gs_log2, unsigned long long* __restrict__ work, int32_t* err) {
   constexpr int ROWB = HD * 2;  // bytes of one K or V row (of the pool's type)
@@ -211,13 +233,13 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
   int32_t* cut = cub + nseq + 1;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const size_t scan_bytes = ((size_t)2 * (nseq + 1) * 4 + 127) & ~(size_t)127;
-  const int WBYTES = STAGES * STAGE + (BITS ? 2 * ATT_CHUNK * ROWB : 0) + (QSMEM ? ATT_CHUNK * ROWB : 0);
+  const int WBYTES = STAGES * STAGE + (BITS ? ATT_CHUNK * ROWB : 0) + (QSMEM ? ATT_CHUNK * ROWB : 0);
   const uint32_t wbuf = (uint32_t)__cvta_generic_to_shared(smem + scan_bytes) + warp * WBYTES;
-  const uint32_t tbuf = wbuf + STAGES * STAGE;                          // dequantised K/V tile
-  const uint32_t qbuf = tbuf + (BITS ? 2 * ATT_CHUNK * ROWB : 0);
+  const uint32_t tbuf = wbuf + STAGES * STAGE;  // dequantised K, then V, of a quantised stage
+  const uint32_t qbuf = tbuf + (BITS ? ATT_CHUNK * ROWB : 0);
   pdl_wait();
   pdl_release();
-  scan_seq_lens(lens, nseq, split, cub, cut);
+  const int split = pick_split(lens, nseq, g.heads, target, cap_splits, cub, cut);
   const int64_t nsplit = cub[nseq];
   if (nsplit > cap_splits) {
     if (threadIdx.x == 0) atomicOr(err, DEV_ERR_WORKSPACE);
@@ -411,46 +433,74 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
       const uint32_t sb = wbuf + (ci % STAGES) * STAGE;
       uint32_t kb = sb, vb = sb + ATT_CHUNK * ROWB;
       const int tc = t_begin + ci * ATT_CHUNK;
-      if (BITS) {
-        // dequantise the stage into the K/V tile; rows past the end are zeros
-        constexpr int GPR = HD / 8;  // 16-byte groups of 8 elements per row
+      // Quantised stage: dequantise K (then, before P V, V) into the tile;
+      // rows past the end are zeros.  A task is 32 elements of one row: its
+      // codes in one or two 16-byte loads, the scale/zero of its group
+      // loaded once per group.
+      auto dequant = [&](int kv) {
+        constexpr int SPR = HD / 32;                        // 32-element segments per row
+        constexpr int CBS = 32 * (BITS == 4 ? 4 : 8) / 8;  // code bytes per segment
         const int nval = min(ATT_CHUNK, t_end - tc);
-        for (int x = lane; x < 2 * ATT_CHUNK * GPR; x += 32) {
-          const int kv = x / (ATT_CHUNK * GPR), rem = x - kv * (ATT_CHUNK * GPR);
-          const int row = rem / GPR, g8 = rem - row * GPR;
-          uint4 w4 = make_uint4(0u, 0u, 0u, 0u);
-          if (row < nval) {
-            const uint32_t raw = sb + kv * RAWH;
-            uint2 cw = make_uint2(0u, 0u);
-            if (BITS == 8) cw = lds64(raw + row * RB + g8 * 8);
-            else cw.x = lds32(raw + row * RB + g8 * 4);
-            const uint32_t ma = raw + ATT_CHUNK * RB + row * MB + ((g8 * 8) >> gs_log2) * (MF32 ? 8 : 4);
-            float sc, zr;
-            if (MF32) {
-              const uint2 m = lds64(ma);
-              sc = __uint_as_float(m.x);
-              zr = __uint_as_float(m.y);
-            } else {
-              const uint32_t m = lds32(ma);
-              const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&m));
-              sc = f.x;
-              zr = f.y;
+#pragma unroll
+        for (int i = 0; i < (ATT_CHUNK * SPR) / 32; ++i) {  // compile-time count: loads of all tasks issued together
+          const int x = lane + 32 * i;
+          const int seg = x % SPR, row = x / SPR;
+          const uint32_t dst = tbuf + row * ROWB;
+          if (row >= nval) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) sts128(dst + (((seg * 4 + k) ^ (row & 7)) << 4), make_uint4(0u, 0u, 0u, 0u));
+            continue;
+          }
+          const uint32_t raw = sb + kv * RAWH;
+          uint32_t cwd[8];
+          {
+            const uint4 a = lds128(raw + row * RB + seg * CBS);
+            cwd[0] = a.x; cwd[1] = a.y; cwd[2] = a.z; cwd[3] = a.w;
+            if (BITS == 8) {
+              const uint4 b = lds128(raw + row * RB + seg * CBS + 16);
+              cwd[4] = b.x; cwd[5] = b.y; cwd[6] = b.z; cwd[7] = b.w;
             }
+          }
+          const uint32_t mrow = raw + ATT_CHUNK * RB + row * MB;
+          float sc = 0.0f, zr = 0.0f;
+          int cur = -1;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {  // 8 elements per k
+            const int pair = (seg * 32 + k * 8) >> gs_log2;
+            if (pair != cur) {
+              cur = pair;
+              if (MF32) {
+                const uint2 m = lds64(mrow + pair * 8);
+                sc = __uint_as_float(m.x);
+                zr = __uint_as_float(m.y);
+              } else {
+                const uint32_t m = lds32(mrow + pair * 4);
+                const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&m));
+                sc = f.x;
+                zr = f.y;
+              }
+            }
+            uint2 cw;
             uint32_t lo4 = 0, hi4 = 0;
-            if (BITS == 4) {
+            if (BITS == 8) {
+              cw = make_uint2(cwd[2 * k], cwd[2 * k + 1]);
+            } else {
+              cw = make_uint2(cwd[k], 0u);
               lo4 = cw.x & 0x0F0F0F0Fu;
               hi4 = (cw.x >> 4) & 0x0F0F0F0Fu;
             }
             float f[8];
 #pragma unroll
             for (int e = 0; e < 8; e += 2) dq_pair<BITS == 4 ? 4 : 8, MF32>(cw, lo4, hi4, e, sc, zr, f[e], f[e + 1]);
-            w4 = make_uint4(pack2<DT>(f[0], f[1]), pack2<DT>(f[2], f[3]), pack2<DT>(f[4], f[5]), pack2<DT>(f[6], f[7]));
+            sts128(dst + (((seg * 4 + k) ^ (row & 7)) << 4),
+                   make_uint4(pack2<DT>(f[0], f[1]), pack2<DT>(f[2], f[3]), pack2<DT>(f[4], f[5]), pack2<DT>(f[6], f[7])));
           }
-          sts128(tbuf + kv * ATT_CHUNK * ROWB + row * ROWB + ((g8 ^ (row & 7)) << 4), w4);
         }
         __syncwarp();
+      };
+      if (BITS) {
+        dequant(0);
         kb = tbuf;
-        vb = tbuf + ATT_CHUNK * ROWB;
       }
 
       // S = Q K^T: two n-tiles of 8 tokens
@@ -512,6 +562,11 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
           o[d][3] *= a1;
         }
       }
+      if (BITS) {
+        __syncwarp();  // every lane has read K from the tile
+        dequant(1);
+        vb = tbuf;
+      }
       // O += P V; P's accumulator layout is the A-fragment layout
       uint32_t pa[4];
       pa[0] = pack2<DT>(sacc[0][0], sacc[0][1]);
@@ -564,7 +619,7 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
 // One warp per (sequence, query head) of the sequences held by two or more
 // splits (the split kernel wrote the others): combine_splits.
 template <int DT, int HD>
-__global__ void __launch_bounds__(256) attn_combine_kernel(const int32_t* __restrict__ lens, int nseq, int split,
+__global__ void __launch_bounds__(256) attn_combine_kernel(const int32_t* __restrict__ lens, int nseq, int64_t target,
                                                            int heads, int G, const float* __restrict__ part_o,
                                                            const float* __restrict__ part_ml, uint8_t* __restrict__ out,
                                                            int64_t cap_splits, unsigned long long* __restrict__ work) {
@@ -574,7 +629,7 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const int32_t* __rest
   // seq_lens is an input of the split kernel, not one of its outputs: the
   // scan may run while that kernel drains; the partials are read after the wait
   pdl_release();
-  scan_seq_lens(lens, nseq, split, cub, cut);
+  pick_split(lens, nseq, heads, target, cap_splits, cub, cut);
   pdl_wait();
   if (blockIdx.x == 0 && threadIdx.x == 0) *work = 0;  // the split kernel has taken all its items
   if (cub[nseq] > cap_splits) return;  // flagged by the split kernel
@@ -600,10 +655,16 @@ namespace {
 // a (max, sum) pair per query head, all f32.
 size_t split_bytes(int heads, int G, int hd) { return (size_t)heads * G * (hd + 2) * sizeof(float); }
 
-using AttnFn = void (*)(PoolGeo, int, const uint8_t*, int, const int32_t*, int, const int32_t*, int, int, float,
-                        float*, float*, int64_t, uint8_t*, int, unsigned long long*, int32_t*);
-using CombineFn = void (*)(const int32_t*, int, int, int, int, const float*, const float*, uint8_t*, int64_t,
+using AttnFn = void (*)(PoolGeo, int, const uint8_t*, int, const int32_t*, int, const int32_t*, int, int64_t,
+                        float, float*, float*, int64_t, uint8_t*, int, unsigned long long*, int32_t*);
+using CombineFn = void (*)(const int32_t*, int, int64_t, int, int, const float*, const float*, uint8_t*, int64_t,
                            unsigned long long*);
+
+// Work items a launch wants (about three per resident warp) before it
+// halves its split size.
+int64_t attn_target(AttnFn fa, size_t smem, int num_sms) {
+  return 3 * (int64_t)persistent_grid(fa, ATT_WARPS * 32, smem, num_sms) * ATT_WARPS;
+}
 
 // The configuration the dispatch uses: stages in flight per warp, CTAs per
 // SM, queries in shared memory.
@@ -611,13 +672,13 @@ constexpr int ATT_STAGES = 2, ATT_MINB = 3;
 constexpr bool ATT_QSMEM = true;
 
 // Dynamic shared memory of one CTA: the scan arrays, then per warp its
-// stages (raw code and meta rows for a quantised pool), the dequantised K/V
-// tile (quantised pools) and the queries (qsmem).
+// stages (raw code and meta rows for a quantised pool), the dequantised K or
+// V tile (quantised pools) and the queries (qsmem).
 size_t attn_smem(int nseq, int hd, int stages, bool qsmem, int bits, int row_bytes, int meta_row_bytes) {
   const size_t scan_bytes = ((size_t)2 * (nseq + 1) * 4 + 127) & ~(size_t)127;
   const size_t rowb = (size_t)hd * 2;
   const size_t stage = bits ? 2 * ATT_CHUNK * (size_t)(row_bytes + meta_row_bytes) : 2 * ATT_CHUNK * rowb;
-  return scan_bytes + (size_t)ATT_WARPS * (stages * stage + (bits ? 2 * ATT_CHUNK * rowb : 0) +
+  return scan_bytes + (size_t)ATT_WARPS * (stages * stage + (bits ? ATT_CHUNK * rowb : 0) +
                                            (qsmem ? ATT_CHUNK * rowb : 0));
 }
 
@@ -630,6 +691,13 @@ AttnFn pick_attn(int bits, bool mf32) {
   return paged_decode_attn_kernel<DT, HD, ATT_STAGES, ATT_MINB, ATT_QSMEM>;
 }
 
+
+AttnFn attn_kernel_of(const rmlx_pool_config& c) {
+  const bool bf = c.dtype == RMLX_BF16, mf32 = c.meta_dtype == RMLX_F32;
+  const int bits = c.quant_bits;
+  return c.head_dim == 128 ? (bf ? pick_attn<RMLX_BF16, 128>(bits, mf32) : pick_attn<RMLX_F16, 128>(bits, mf32))
+                           : (bf ? pick_attn<RMLX_BF16, 64>(bits, mf32) : pick_attn<RMLX_F16, 64>(bits, mf32));
+}
 }  // namespace
 
 extern "C" {
@@ -639,8 +707,21 @@ rmlx_status rmlx_kv_attention_workspace_size(const rmlx_kv_pool* p, int32_t q_he
   if (!p || !bytes) return fail(RMLX_E_BAD_ARG, "NULL pool or bytes");
   if (q_heads_per_kv < 1 || q_heads_per_kv > 16) return fail(RMLX_E_BAD_ARG, "q_heads_per_kv must be in [1, 16]");
   if (num_seqs < 0 || max_total_tokens < 0) return fail(RMLX_E_BAD_ARG, "negative num_seqs or max_total_tokens");
-  const int64_t splits = max_total_tokens / ATT_SPLIT + num_seqs;
-  *bytes = (size_t)splits * split_bytes(p->cfg.num_kv_heads, q_heads_per_kv, p->cfg.head_dim);
+  const rmlx_pool_config& c = p->cfg;
+  int64_t splits = max_total_tokens / ATT_SPLIT + num_seqs;
+  if ((c.dtype == RMLX_F16 || c.dtype == RMLX_BF16) && (c.head_dim == 64 || c.head_dim == 128)) {
+    // room for the smaller splits a launch with few work items takes (down
+    // to 64 tokens: at most 4x the splits of a launch below the target)
+    AttnFn fa = attn_kernel_of(c);
+    const size_t smem = attn_smem(num_seqs, c.head_dim, ATT_STAGES, ATT_QSMEM, c.quant_bits, (int)p->row_bytes,
+                                  (int)p->meta_row_bytes);
+    DeviceGuard dg(p->device);
+    if (smem <= 227 * 1024 && prepare_smem(fa, smem) == RMLX_OK) {
+      const int64_t target = attn_target(fa, smem, p->num_sms);
+      splits = std::max<int64_t>(splits, 4 * ((target + c.num_kv_heads - 1) / c.num_kv_heads) + num_seqs);
+    }
+  }
+  *bytes = (size_t)splits * split_bytes(c.num_kv_heads, q_heads_per_kv, c.head_dim);
   return RMLX_OK;
 }
 
@@ -673,9 +754,7 @@ rmlx_status rmlx_kv_decode_attention(rmlx_kv_pool* p, int32_t layer, const void*
   cudaStream_t st = (cudaStream_t)stream;
   const bool bf = c.dtype == RMLX_BF16;
   const int bits = c.quant_bits;
-  const bool mf32 = c.meta_dtype == RMLX_F32;
-  AttnFn fa = hd == 128 ? (bf ? pick_attn<RMLX_BF16, 128>(bits, mf32) : pick_attn<RMLX_F16, 128>(bits, mf32))
-                        : (bf ? pick_attn<RMLX_BF16, 64>(bits, mf32) : pick_attn<RMLX_F16, 64>(bits, mf32));
+  AttnFn fa = attn_kernel_of(c);
   CombineFn fc = hd == 128 ? (bf ? attn_combine_kernel<RMLX_BF16, 128> : attn_combine_kernel<RMLX_F16, 128>)
                            : (bf ? attn_combine_kernel<RMLX_BF16, 64> : attn_combine_kernel<RMLX_F16, 64>);
   if (!p->attn_work) {  // the item counter: pool memory, zero between launches
@@ -691,17 +770,18 @@ rmlx_status rmlx_kv_decode_attention(rmlx_kv_pool* p, int32_t layer, const void*
   rmlx_status s;
   if ((s = prepare_smem(fa, smem)) != RMLX_OK) return s;
   const int grid = persistent_grid(fa, ATT_WARPS * 32, smem, p->num_sms);
+  const int64_t target = attn_target(fa, smem, p->num_sms);
   const float scale_log2 = softmax_scale * 1.4426950408889634f;  // log2(e)
   cudaError_t e = launch_pdl(fa, dim3(grid), dim3(ATT_WARPS * 32), smem, st, p->geo(), (int)layer,
                              static_cast<const uint8_t*>(q), G, block_tables, (int)block_table_stride, seq_lens,
-                             (int)num_seqs, ATT_SPLIT, scale_log2, part_o, part_ml, cap, static_cast<uint8_t*>(out),
+                             (int)num_seqs, target, scale_log2, part_o, part_ml, cap, static_cast<uint8_t*>(out),
                              bits ? log2i(c.group_size) : 0, p->attn_work, p->err);
   if (e != cudaSuccess) return cuda_check(e, "decode attention launch");
   const size_t csmem = (size_t)2 * (num_seqs + 1) * 4;
   if ((s = prepare_smem(fc, csmem)) != RMLX_OK) return s;
   const int64_t warps = (int64_t)num_seqs * heads * G;
   const int cgrid = (int)std::min<int64_t>((warps + 7) / 8, (int64_t)p->num_sms * 8);
-  e = launch_pdl(fc, dim3(cgrid), dim3(256), csmem, st, seq_lens, (int)num_seqs, ATT_SPLIT, heads, G, part_o,
+  e = launch_pdl(fc, dim3(cgrid), dim3(256), csmem, st, seq_lens, (int)num_seqs, target, heads, G, part_o,
                  part_ml, static_cast<uint8_t*>(out), cap, p->attn_work);
   if (e != cudaSuccess) {
     cudaMemsetAsync(p->attn_work, 0, 16, st);  // the combine would have reset the counter

@@ -127,7 +127,7 @@ def test_workspace_too_small_is_flagged(cuda):
     bt, _ = block_tables(rng, lens, 16, 64)
     q = torch.zeros((2, 8, 128), dtype=torch.bfloat16, device=cuda)
     need = pool.attention_workspace_size(4, 2, 900)
-    small = pool.attention_workspace_size(4, 0, 256)  # room for one split only
+    small = 2 * 4 * (128 + 2) * 4  # one split: 2 KV heads x 4 query heads x (head_dim + max, sum) f32
     assert 0 < small < need
     ws = torch.empty(small, dtype=torch.uint8, device=cuda)
     out = torch.full((2, 8, 128), 3.0, dtype=torch.bfloat16, device=cuda)
