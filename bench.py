@@ -66,6 +66,9 @@ class Workload:
     meta: int = F16
     outliers: float = 0.0
     attn_g: int = 0  # > 0: decode attention with this many query heads per KV head instead of the gather
+    dtype: int = BF16
+    lens: tuple = ()  # fixed prompt lengths (instead of uniform in [ctx_lo, ctx_hi])
+    min_blocks: int = 0  # pool at least this large
 
     # bytes of one token's rows of the local heads
     def in_row(self, h):
@@ -105,6 +108,11 @@ WORKLOADS = {
         "scale/zero, batch 128, ctx U[1024,8192], 1% outliers x8; quantise-on-append 1 token/seq/layer, then "
         "dequantise-on-gather (bf16) of every layer", seed=0x5EED + 3, batch=128, ctx_lo=1024, ctx_hi=8192, bits=4,
         outliers=0.01),
+    "config1": Workload(
+        "config1", "KV append+gather HBM GB/s (1 layer, 4 sequences; latency-bound: see us_per_step)",
+        "the reference's own case: 1 layer x 8 KV heads x 128, block 16, fp16, pool 256 blocks, 4 sequences with "
+        "prompts 37/128/255/512, 1 token appended per sequence per step, then the gather of the layer",
+        seed=0x5EED + 1, layers=1, batch=4, lens=(37, 128, 255, 512), dtype=F16, min_blocks=256),
     "attn": Workload(
         "attn", "KV append + paged decode attention HBM GB/s (decode step, Llama-3.1-8B shape)",
         "decode step with attention reading the pool in place: 32 layers x 8 KV heads x 128, block 16, bf16, "
@@ -487,9 +495,12 @@ def make_workload(w, steps_total):
     per-step slot mappings for `steps_total` steps."""
     import rmlx_kv
     rng = np.random.default_rng(w.seed)
-    lens0 = rng.integers(w.ctx_lo, w.ctx_hi + 1, size=w.batch).astype(np.int64)
+    if w.lens:
+        lens0 = np.array(w.lens, dtype=np.int64)
+    else:
+        lens0 = rng.integers(w.ctx_lo, w.ctx_hi + 1, size=w.batch).astype(np.int64)
     need = (lens0 + steps_total + w.block - 1) // w.block
-    num_blocks = int(np.ceil(1.25 * need.sum()))
+    num_blocks = max(int(np.ceil(1.25 * need.sum())), w.min_blocks)
     mgr = rmlx_kv.PagedCacheManager(w.block, num_blocks)
     # Make the free list a seeded permutation of the pool: allocate all, free
     # in permuted order (FIFO reuse hands them out in that order).
@@ -651,7 +662,7 @@ def run_reference(args, w, rank, world):
     print(json.dumps({
         "impl": "reference", "metric": w.metric, "value": round(gbs, 2), "unit": "GB/s", "n_gpus": world,
         "steps": steps, "warmup": warm, "ms_per_step": round(sec * w.layers * 1e3, 3), "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "scaling": "strong", "vs_baseline": None, "dtype": "f16" if w.dtype == F16 else "bf16", "data": "synthetic",
         "config": config_of(w, w.heads, wl["num_blocks"], 1),
         "cpu_baseline": {"value": round(gbs, 2), "unit": "GB/s", "cores": threads, "kind": "port",
                          "sample": sample},
@@ -662,7 +673,8 @@ def run_reference(args, w, rank, world):
 def config_of(w, H, num_blocks, world):
     c = {"workload": w.desc, "batch": w.batch, "layers": w.layers, "kv_heads": w.heads, "kv_heads_per_gpu": H,
          "head_dim": w.head_dim, "block_size": w.block, "pool_blocks": num_blocks, "sharding": f"kv-head x{world}",
-         "l2": "inputs larger than L2: each gather launch moves >0.1 GB, no flush"}
+         "l2": ("inputs larger than L2: each gather launch moves >0.1 GB, no flush" if not w.lens else
+                "L2-resident (a few MB per step): a latency-bound case, reported as us_per_step")}
     if w.bits:
         c.update({"quant_bits": w.bits, "group_size": w.group, "meta": "f16" if w.meta == F16 else "f32",
                   "outliers": w.outliers})
@@ -747,7 +759,8 @@ def main():
     wl = make_workload(w, W + K)
     lens0, bt, slots, num_blocks = wl["lens0"], wl["bt"], wl["slots"], wl["num_blocks"]
 
-    pool = rmlx_kv.KVPool(L, H, D, BS, num_blocks, dtype=rmlx_kv.BF16, quant_bits=w.bits, group_size=w.group,
+    tdt = torch.float16 if w.dtype == F16 else torch.bfloat16
+    pool = rmlx_kv.KVPool(L, H, D, BS, num_blocks, dtype=w.dtype, quant_bits=w.bits, group_size=w.group,
                           meta_dtype=w.meta, head_offset=rank * H, device=dev)
     h = pool.handle
     lib = _lib.lib
@@ -759,7 +772,7 @@ def main():
         x = torch.randn(shape, device="cuda", dtype=torch.float32, generator=gen)
         if w.outliers:
             x = torch.where(torch.rand(shape, device="cuda", generator=gen) < w.outliers, x * 8.0, x)
-        return x.to(torch.bfloat16)
+        return x.to(tdt)
 
     ts, hs = H * D, D
     bt_d = torch.from_numpy(bt).cuda()
@@ -777,7 +790,7 @@ def main():
                                           sp))
         del kk, vv
     else:
-        view = torch.as_tensor(DevView(pool.layout.base, pool.layout.bytes), device="cuda").view(torch.bfloat16)
+        view = torch.as_tensor(DevView(pool.layout.base, pool.layout.bytes), device="cuda").view(tdt)
         step = 1 << 28
         for o in range(0, view.numel(), step):
             view[o:o + step].normal_(generator=gen)
@@ -792,13 +805,13 @@ def main():
     if G:
         # per-layer queries of the step, attention output, split workspace
         q_d = rand_rows((L, B, H * G, D))
-        att_out = torch.empty((B, H * G, D), device="cuda", dtype=torch.bfloat16)
+        att_out = torch.empty((B, H * G, D), device="cuda", dtype=tdt)
         ws_bytes = pool.attention_workspace_size(G, B, int(lens_steps[-1].sum()))
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
         scale = 1.0 / float(np.sqrt(D))
         out_k = out_v = None
     else:
-        out_k = torch.empty(int(lens_steps[-1].sum()) * H * D, device="cuda", dtype=torch.bfloat16)
+        out_k = torch.empty(int(lens_steps[-1].sum()) * H * D, device="cuda", dtype=tdt)
         out_v = torch.empty_like(out_k)
     ls = B * H * D
 
@@ -897,14 +910,14 @@ def main():
         planner.add(int(uids[s]), rng.integers(0, 128256, size=int(lens0[s]) + W, dtype=np.uint32))
     step_tokens = rng.integers(0, 128256, size=(K, B), dtype=np.uint32)
     host_bt = np.zeros_like(bt)
-    pin_k = torch.empty((K, L, B, H, D), dtype=torch.bfloat16, pin_memory=True)
+    pin_k = torch.empty((K, L, B, H, D), dtype=tdt, pin_memory=True)
     pin_v = torch.empty_like(pin_k, pin_memory=True)
     pin_k.copy_(new_k[W:W + K].cpu())
     pin_v.copy_(new_v[W:W + K].cpu())
     pin_bt = torch.from_numpy(host_bt).pin_memory()
     pin_slots = torch.empty(B, dtype=torch.int32, pin_memory=True)
     pin_lens = torch.empty(B, dtype=torch.int32, pin_memory=True)
-    dk = torch.empty((L, B, H, D), device="cuda", dtype=torch.bfloat16)
+    dk = torch.empty((L, B, H, D), device="cuda", dtype=tdt)
     dv = torch.empty_like(dk)
     d_slots = torch.empty(B, dtype=torch.int32, device="cuda")
     d_lens = torch.empty(B, dtype=torch.int32, device="cuda")
@@ -964,7 +977,8 @@ def main():
         print(json.dumps({
             "metric": w.metric, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": K,
             "warmup": W, "ms_per_step": round(ms_per_step, 4), "us_per_step": round(ms_per_step * 1e3, 1),
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f16" if w.dtype == F16 else "bf16",
             "data": "synthetic", "config": config_of(w, H, num_blocks, world),
             "roofline": {"bound": "hbm", "kernel": w.kernel, "achieved": round(achieved, 1), "peak": peak,
                          "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),

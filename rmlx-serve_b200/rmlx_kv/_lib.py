@@ -25,6 +25,11 @@ OK, E_RANGE, E_DOUBLE_FREE, E_OVERFLOW, E_FREE_BLOCK, E_BAD_ARG, E_EXHAUSTED, \
 F32, F16, BF16 = 0, 1, 2
 
 
+# rmlx_status values (include/rmlx_kv.h)
+RMLX_OK, RMLX_E_RANGE, RMLX_E_DOUBLE_FREE, RMLX_E_OVERFLOW, RMLX_E_FREE_BLOCK, RMLX_E_BAD_ARG = 0, 1, 2, 3, 4, 5
+RMLX_E_EXHAUSTED, RMLX_E_CUDA, RMLX_E_NCCL, RMLX_E_TIMEOUT, RMLX_E_DEVICE = 6, 7, 8, 9, 10
+
+
 class RmlxError(RuntimeError):
     def __init__(self, status: int, msg: str):
         super().__init__(f"{msg} [{lib.rmlx_status_string(status).decode()}]")
