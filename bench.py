@@ -83,7 +83,7 @@ class Workload:
     @property
     def kernel(self):
         if self.attn_g:
-            return "paged_decode_attn_kernel"
+            return "paged_decode_attn_codes_kernel" if self.bits else "paged_decode_attn_kernel"
         return "gather_dequant_r1_kernel" if self.bits else "gather_rows_kernel"
 
     @property
@@ -122,8 +122,14 @@ WORKLOADS = {
         "attn8", "KV quant-append + paged decode attention over 8-bit codes HBM GB/s (decode step, Llama-3.1-8B shape)",
         "decode step with attention reading an 8-bit pool in place: 32 layers x 8 KV heads x 128, block 16, 8-bit "
         "codes, group 64, fp16 scale/zero, 32 query heads (4 per KV head), batch 64, ctx U[512,4096]; quantise-on-"
-        "append 1 token/seq/layer, then paged decode attention of every layer (codes dequantised in shared memory)",
+        "append 1 token/seq/layer, then paged decode attention of every layer (codes fed to the tensor cores)",
         seed=0x5EED + 2, attn_g=4, bits=8),
+    "attn4": Workload(
+        "attn4", "KV quant-append + paged decode attention over 4-bit codes HBM GB/s (decode step, Llama-3.1-8B shape)",
+        "decode step with attention reading a 4-bit pool in place: 32 layers x 8 KV heads x 128, block 16, 4-bit "
+        "codes (2 per byte), group 64, fp16 scale/zero, 32 query heads (4 per KV head), batch 64, ctx U[512,4096]; "
+        "quantise-on-append 1 token/seq/layer, then paged decode attention of every layer (codes fed to the tensor "
+        "cores)", seed=0x5EED + 2, attn_g=4, bits=4),
 }
 
 

@@ -197,6 +197,106 @@ __device__ __forceinline__ int pick_split(const int32_t* lens, int nseq, int hea
   return split;
 }
 
+// 16-byte column `ch` of staged code row t.  SWZ = 0: rows as they lie in
+// the tile.  SWZ = columns per row: XOR-swizzled so that the 8 row
+// addresses of an ldmatrix (8 consecutive rows, one column) fall in 8
+// different 16-byte bank groups.
+template <int SWZ>
+__device__ __forceinline__ int code_col(int t, int ch) {
+  if (SWZ == 0) return ch;
+  return SWZ >= 8 ? ch ^ (t & 7) : ch ^ (((t * SWZ) >> 3) & (SWZ - 1));
+}
+
+// Stages the raw rows of tokens tc .. tc+15 of KV head h of a quantised
+// pool: at dst the 16 K code rows (row_bytes each, columns placed by
+// code_col<SWZ>) then the 16 K scale/zero rows, and the same for V at dst +
+// 16 x (row_bytes + meta_row_bytes).  A chunk inside one block copies its 16
+// rows as they are (rows past the sequence's end included); otherwise rows
+// are located one by one and rows past t_end, like those of a bad block
+// (flagged), are zeros.  Commits one cp.async group.
+template <int SWZ>
+__device__ __forceinline__ void load_quant_chunk(uint32_t dst, const PoolGeo& g, int layer, int h,
+                                                 const int32_t* btrow, int tc, int t_end, bool aligned_blocks,
+                                                 int64_t vdelta, int lane, int32_t* err) {
+  constexpr unsigned FULL = 0xffffffffu;
+  const int RB = SWZ ? SWZ * 16 : g.row_bytes, MB = g.meta_row_bytes;
+  const int RAWH = ATT_CHUNK * (RB + MB);
+  const int cpr = SWZ ? SWZ : RB / 16;
+  if (aligned_blocks) {
+    // 16 code rows and 16 meta rows, each a contiguous run of the tile
+    const int32_t blk = __ldg(btrow + tc / g.bs);
+    const bool ok = blk >= 0 && blk < g.nblocks;
+    if (!ok && lane == 0) atomicOr(err, DEV_ERR_BLOCK);
+    const int n = ok ? 16 : 0;
+    const uint8_t* tile = ok ? g.base + g.tile_off(blk, layer, 0, h) : g.base;
+    const int r0 = tc % g.bs;
+    const uint8_t* codes = tile + (int64_t)r0 * RB;
+    const uint8_t* meta = tile + (int64_t)g.bs * RB + (int64_t)r0 * MB;
+    const int cc = ATT_CHUNK * cpr, mc = ATT_CHUNK * MB / 16;
+    for (int x = lane; x < cc + mc; x += 32) {
+      const bool isc = x < cc;
+      const int off = (isc ? x : x - cc) * 16;
+      const uint8_t* sp = n ? (isc ? codes : meta) + off : g.base;
+      uint32_t so;
+      if (isc) {
+        const int row = x / cpr;
+        so = row * RB + (code_col<SWZ>(row, x - row * cpr) << 4);
+      } else {
+        so = ATT_CHUNK * RB + off;
+      }
+      cp_async16(dst + so, sp, n);
+      cp_async16(dst + RAWH + so, n ? sp + vdelta : g.base, n);
+    }
+  } else {
+    // rows from different blocks: one row's codes and meta at a time
+    const int t = tc + (lane & 15);
+    const uint8_t* tile = g.base;
+    int nb = 0;
+    if (t < t_end) {
+      const int32_t blk = __ldg(btrow + t / g.bs);
+      if (blk >= 0 && blk < g.nblocks) {
+        tile = g.base + g.tile_off(blk, layer, 0, h);
+        nb = 1;
+      } else if (lane < 16) {
+        atomicOr(err, DEV_ERR_BLOCK);
+      }
+    }
+    const int rw = t % g.bs;
+    const unsigned long long cp_ = reinterpret_cast<unsigned long long>(tile + (int64_t)rw * RB);
+    const unsigned long long mp_ = reinterpret_cast<unsigned long long>(tile + (int64_t)g.bs * RB + (int64_t)rw * MB);
+    const int mcs = MB < 16 ? MB : 16, mpr = MB / mcs;
+    // each row's pointers by shuffle (all lanes), then its copies
+    for (int row = 0; row < ATT_CHUNK; ++row) {
+      const int ok = __shfl_sync(FULL, nb, row);
+      const uint8_t* rc = reinterpret_cast<const uint8_t*>(__shfl_sync(FULL, cp_, row));
+      const uint8_t* rm = reinterpret_cast<const uint8_t*>(__shfl_sync(FULL, mp_, row));
+      for (int k = lane; k < cpr + mpr; k += 32) {
+        if (k < cpr) {
+          const uint32_t so = row * RB + (code_col<SWZ>(row, k) << 4);
+          cp_async16(dst + so, ok ? rc + k * 16 : g.base, ok ? 16 : 0);
+          cp_async16(dst + RAWH + so, ok ? rc + vdelta + k * 16 : g.base, ok ? 16 : 0);
+        } else {
+          const int m = k - cpr;
+          const uint32_t so = ATT_CHUNK * RB + row * MB + m * mcs;
+          const uint8_t* a = ok ? rm + m * mcs : g.base;
+          const uint8_t* b = ok ? rm + vdelta + m * mcs : g.base;
+          if (mcs == 16) {
+            cp_async16(dst + so, a, ok ? 16 : 0);
+            cp_async16(dst + RAWH + so, b, ok ? 16 : 0);
+          } else if (mcs == 8) {
+            cp_async8(dst + so, a, ok ? 8 : 0);
+            cp_async8(dst + RAWH + so, b, ok ? 8 : 0);
+          } else {
+            cp_async4(dst + so, a, ok ? 4 : 0);
+            cp_async4(dst + RAWH + so, b, ok ? 4 : 0);
+          }
+        }
+      }
+    }
+  }
+  cp_async_commit();
+}
+
 // Shared-memory layout of one stage: K rows then V rows of a 16-token chunk,
 // row-major, 16-byte column chunk c of row r stored at slot c ^ (r & 7) so
 // that the 8 row addresses of every ldmatrix hit 8 different bank groups.
@@ -303,73 +403,7 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
       const uint32_t dst = wbuf + (ci % STAGES) * STAGE;
       const int tc = t_begin + ci * ATT_CHUNK;
       if (BITS) {
-        if (aligned_blocks) {
-          // 16 code rows and 16 meta rows, each a contiguous run of the tile
-          const int32_t blk = __ldg(btrow + tc / g.bs);
-          const bool ok = blk >= 0 && blk < g.nblocks;
-          if (!ok && lane == 0) atomicOr(err, DEV_ERR_BLOCK);
-          const int n = ok ? 16 : 0;
-          const uint8_t* tile = ok ? g.base + g.tile_off(blk, layer, 0, h) : g.base;
-          const int r0 = tc % g.bs;
-          const uint8_t* codes = tile + (int64_t)r0 * RB;
-          const uint8_t* meta = tile + (int64_t)g.bs * RB + (int64_t)r0 * MB;
-          const int cc = ATT_CHUNK * RB / 16, mc = ATT_CHUNK * MB / 16;
-          for (int x = lane; x < cc + mc; x += 32) {
-            const bool isc = x < cc;
-            const int off = (isc ? x : x - cc) * 16;
-            const uint8_t* sp = n ? (isc ? codes : meta) + off : g.base;
-            const uint32_t so = (isc ? 0 : ATT_CHUNK * RB) + off;
-            cp_async16(dst + so, sp, n);
-            cp_async16(dst + RAWH + so, n ? sp + vdelta : g.base, n);
-          }
-        } else {
-          // rows from different blocks: one row's codes and meta at a time
-          const int t = tc + (lane & 15);
-          const uint8_t* tile = g.base;
-          int nb = 0;
-          if (t < t_end) {
-            const int32_t blk = __ldg(btrow + t / g.bs);
-            if (blk >= 0 && blk < g.nblocks) {
-              tile = g.base + g.tile_off(blk, layer, 0, h);
-              nb = 1;
-            } else if (lane < 16) {
-              atomicOr(err, DEV_ERR_BLOCK);
-            }
-          }
-          const int rw = t % g.bs;
-          const unsigned long long cp_ = reinterpret_cast<unsigned long long>(tile + (int64_t)rw * RB);
-          const unsigned long long mp_ = reinterpret_cast<unsigned long long>(tile + (int64_t)g.bs * RB + (int64_t)rw * MB);
-          const int cpr = RB / 16, mcs = MB < 16 ? MB : 16, mpr = MB / mcs;
-          // each row's pointers by shuffle (all lanes), then its copies
-          for (int row = 0; row < ATT_CHUNK; ++row) {
-            const int ok = __shfl_sync(FULL, nb, row);
-            const uint8_t* rc = reinterpret_cast<const uint8_t*>(__shfl_sync(FULL, cp_, row));
-            const uint8_t* rm = reinterpret_cast<const uint8_t*>(__shfl_sync(FULL, mp_, row));
-            for (int k = lane; k < cpr + mpr; k += 32) {
-              if (k < cpr) {
-                const uint32_t so = row * RB + k * 16;
-                cp_async16(dst + so, ok ? rc + k * 16 : g.base, ok ? 16 : 0);
-                cp_async16(dst + RAWH + so, ok ? rc + vdelta + k * 16 : g.base, ok ? 16 : 0);
-              } else {
-                const int m = k - cpr;
-                const uint32_t so = ATT_CHUNK * RB + row * MB + m * mcs;
-                const uint8_t* a = ok ? rm + m * mcs : g.base;
-                const uint8_t* b = ok ? rm + vdelta + m * mcs : g.base;
-                if (mcs == 16) {
-                  cp_async16(dst + so, a, ok ? 16 : 0);
-                  cp_async16(dst + RAWH + so, b, ok ? 16 : 0);
-                } else if (mcs == 8) {
-                  cp_async8(dst + so, a, ok ? 8 : 0);
-                  cp_async8(dst + RAWH + so, b, ok ? 8 : 0);
-                } else {
-                  cp_async4(dst + so, a, ok ? 4 : 0);
-                  cp_async4(dst + RAWH + so, b, ok ? 4 : 0);
-                }
-              }
-            }
-          }
-        }
-        cp_async_commit();
+        load_quant_chunk<0>(dst, g, layer, h, btrow, tc, t_end, aligned_blocks, vdelta, lane, err);
         return;
       }
       if (aligned_blocks) {
@@ -616,6 +650,515 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Quantised pools read as codes (8-bit with group_size >= 16, 4-bit with
+// group_size >= 32).  Instead of dequantising K and V into a tile, the warp
+// feeds the tensor cores the codes themselves, as exact f16 integers built
+// in registers from the staged code rows, and applies each token's
+// per-group scale s and zero z around the products.  The products are
+// transposed against the kernel above: tokens are the M rows and the query
+// heads the N columns (G <= 8: one 8-wide n-tile; up to 16: two), so a
+// 16-token chunk costs one MMA per k-step instead of two:
+//   S^T = K Q^T:  S^T[t][j] = sum over groups g of
+//                 s_tg (C_tg . q'_jg) + z_tg (sum of q'_jg),
+//   O^T += V^T P^T:  O^T[d][j] += smax_g ((C_g^T (P^T o s_g / smax_g))[d][j]
+//                                  + (sum_t P[j][t] z_tg) / smax_g)
+// with q' = q / max|q| of its row in f16 (the factor returns in the softmax
+// scale) and smax_g the chunk's largest |s_tg| (the f16 weights P s / smax
+// stay in [-1, 1] whatever the scales).  Codes enter centred (code -
+// 2^(bits-1), exact f16 integers) and the zeros as z + 2^(bits-1) s, which
+// halves the magnitude of s * code and with it the weights' rounding.
+//
+// Fragments come straight from the staged code rows (16-byte columns
+// XOR-swizzled, read with ldmatrix):
+//   * K, non-transposed: a lane receives 4 code bytes of token r (or r + 8);
+//     they serve as the lane's k positions {2c, 2c+1, 2c+8, 2c+9} of one
+//     k-step (8-bit) or of two k-steps (4-bit), and the queries, held as B
+//     fragments in registers for the whole item, take their dimensions in
+//     the same order, so the dot products are unchanged;
+//   * V, transposed: a lane receives tokens (2c, 2c+1) x 2 code bytes, which
+//     become A rows r and r + 8 of one m-tile (8-bit: dims 2r, 2r+1 of the
+//     column) or of two (4-bit: dims 4r .. 4r+3); the output is written
+//     back in dimension order;
+//   * P^T o s: the S^T accumulators (token r, heads 2c, 2c+1) scaled per
+//     token, packed to f16 and transposed in registers (movmatrix) into the
+//     B fragments (tokens 2c, 2c+1, head r).
+// A group spans whole k-steps and whole code columns, hence the floor on
+// the group size.
+
+// Two code bytes of w (selector 0x4j4i: bytes i, j) as centred f16
+// integers: 1024 + code is an f16 whose low mantissa byte is the code;
+// 1152 = 1024 + 128 is subtracted.
+__device__ __forceinline__ uint32_t codes8(uint32_t w, uint32_t sel) {
+  const uint32_t x = __byte_perm(w, 0x64646464u, sel);
+  __half2 h = *reinterpret_cast<const __half2*>(&x);
+  const __half2 m = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));
+  h = __hsub2(h, m);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+// Eight 4-bit codes of w as four centred f16x2 pairs: low nibbles of bytes
+// 0 and 2, high nibbles of bytes 0 and 2, then the same of bytes 1 and 3.
+// A low nibble rides on 1024 (ulp 1), a high nibble, in place, on 64 (ulp
+// 1/16); 1032 and 72 are subtracted.
+__device__ __forceinline__ void codes4(uint32_t w, uint32_t (&p)[4]) {
+  const __half2 lo = __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408));
+  const __half2 hi = __halves2half2(__ushort_as_half(0x5480), __ushort_as_half(0x5480));
+  const uint32_t w8 = w >> 8;
+  const uint32_t x[4] = {(w & 0x000F000Fu) | 0x64006400u, (w & 0x00F000F0u) | 0x54005400u,
+                         (w8 & 0x000F000Fu) | 0x64006400u, (w8 & 0x00F000F0u) | 0x54005400u};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __half2 h = __hsub2(*reinterpret_cast<const __half2*>(&x[i]), (i & 1) ? hi : lo);
+    p[i] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+}
+
+// An 8x8 matrix of 16-bit elements held as ldmatrix holds it (lane 4i + j:
+// row i, elements 2j, 2j+1), transposed.
+__device__ __forceinline__ uint32_t movmatrix_t(uint32_t a) {
+  uint32_t d;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));
+  return d;
+}
+
+// D = A B + C with separate C registers (f16 inputs, f32 accumulation).
+__device__ __forceinline__ void mma16816_c(float* d, const uint32_t* a, uint32_t b0, uint32_t b1, float c0, float c1,
+                                           float c2, float c3) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%10,%11,%12,%13};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(c0), "f"(c1), "f"(c2), "f"(c3));
+}
+
+constexpr int CQ_QS_BYTES = 512;  // per warp: sums of the queries per (group, head), 8 x 16 f32
+
+template <int DT, int HD, int BITS, bool MF32, int NH, int STAGES, int MINB>
+__global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
+    paged_decode_attn_codes_kernel(PoolGeo g, int layer, const uint8_t* __restrict__ q, int G,
+                                   const int32_t* __restrict__ bt, int bt_stride, const int32_t* __restrict__ lens,
+                                   int nseq, int64_t target, float scale_log2, float* __restrict__ part_o,
+                                   float* __restrict__ part_ml, int64_t cap_splits, uint8_t* __restrict__ out,
+                                   int gs_log2, unsigned long long* __restrict__ work, int32_t* err) {
+  constexpr int ROWB = HD * 2;             // bytes of a query or output row
+  constexpr int CPR = ROWB / 16;
+  constexpr int RB = HD * BITS / 8;        // bytes of a code row
+  constexpr int NSEG = RB / 16;            // 16-byte code columns per row
+  constexpr int SEGD = 128 / BITS;         // dimensions per code column
+  constexpr int KT = HD / 16;              // k-steps of S^T
+  constexpr int MPS = BITS == 8 ? 1 : 2;   // m-tiles of O^T (16 dims) per code column; k-steps per column
+  constexpr int MT = NSEG * MPS;           // m-tiles of O^T
+  constexpr int CU = ATT_CHUNK * NSEG / 32;  // 16-byte code units per lane per chunk, K or V
+  constexpr unsigned FULL = 0xffffffffu;
+  static_assert(NSEG % 2 == 0 && CU >= 1 && (BITS == 8 || BITS == 4) && (NH == 1 || NH == 2), "shape");
+  const int MB = g.meta_row_bytes;
+  const int RAWH = ATT_CHUNK * (RB + MB);  // K (or V) part of a stage
+  const int STAGE = 2 * RAWH;
+  const int gs = 1 << gs_log2;
+  extern __shared__ __align__(128) uint8_t smem[];
+  int32_t* cub = reinterpret_cast<int32_t*>(smem);
+  int32_t* cut = cub + nseq + 1;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const size_t scan_bytes = ((size_t)2 * (nseq + 1) * 4 + 127) & ~(size_t)127;
+  const int WBYTES = STAGES * STAGE + CQ_QS_BYTES;
+  uint8_t* wgen = smem + scan_bytes + (size_t)warp * WBYTES;
+  const uint32_t wbuf = (uint32_t)__cvta_generic_to_shared(wgen);
+  float* qgs = reinterpret_cast<float*>(wgen + STAGES * STAGE);  // [group][head]
+  pdl_wait();
+  pdl_release();
+  const int split = pick_split(lens, nseq, g.heads, target, cap_splits, cub, cut);
+  const int64_t nsplit = cub[nseq];
+  if (nsplit > cap_splits) {
+    if (threadIdx.x == 0) atomicOr(err, DEV_ERR_WORKSPACE);
+    return;
+  }
+  const int64_t items = nsplit * g.heads;
+  const int qheads = g.heads * G;
+  for (int64_t s0 = (int64_t)blockIdx.x * ATT_WARPS + warp; s0 < nseq; s0 += (int64_t)gridDim.x * ATT_WARPS)
+    if (cut[s0 + 1] == cut[s0]) {
+      uint4* o4 = reinterpret_cast<uint4*>(out + s0 * qheads * ROWB);
+      for (int x = lane; x < qheads * CPR; x += 32) o4[x] = make_uint4(0u, 0u, 0u, 0u);
+    }
+  const int r = lane >> 2, c = lane & 3, mi = lane >> 3;
+  const int trow = ((mi & 1) << 3) + (lane & 7);  // the token row this lane addresses in ldmatrix
+  const int64_t vdelta = (int64_t)g.heads * g.tile_bytes;
+  const bool aligned_blocks = (g.bs % ATT_CHUNK) == 0;
+  auto next_item = [&]() -> int64_t {
+    unsigned long long v = 0;
+    if (lane == 0) v = atomicAdd(work, 1ULL);
+    return (int64_t)__shfl_sync(FULL, v, 0);
+  };
+  for (int64_t it = next_item(); it < items; it = next_item()) {
+    const int h = (int)(it % g.heads);
+    const int64_t sg = it / g.heads;
+    const int s = find_seq(cub, nseq, sg);
+    const int t_begin = (int)(sg - cub[s]) * split;
+    const int t_end = min(cut[s + 1] - cut[s], t_begin + split);
+    const int nchunks = (t_end - t_begin + ATT_CHUNK - 1) / ATT_CHUNK;
+    const int32_t* btrow = bt + (int64_t)s * bt_stride;
+
+    // Queries as B fragments: n-tile n, k-step kk holds head 8n + r at k
+    // positions (2c, 2c+1) and (2c+8, 2c+9); the sums per (group, head)
+    // go to shared memory.
+    uint32_t qb[NH][KT][2];
+    float fsc[NH][2];  // softmax scale x max|q| of heads 8n + 2c + e
+    __syncwarp();  // the previous item's reads of qgs are done
+#pragma unroll
+    for (int n = 0; n < NH; ++n) {
+      const int hr = 8 * n + r;
+      const uint8_t* qrow = q + ((int64_t)s * qheads + (int64_t)h * G + hr) * ROWB;
+      constexpr int NV = HD / 4;  // dimensions per lane: 8-bit 16kk + 4c + (0..3); 4-bit 32j + 8c + (0..7)
+      float f[NV];
+      if (BITS == 8) {
+#pragma unroll
+        for (int kk = 0; kk < KT; ++kk) {
+          const uint2 v = hr < G ? __ldg(reinterpret_cast<const uint2*>(qrow + (16 * kk + 4 * c) * 2)) : make_uint2(0u, 0u);
+          const uint32_t w[2] = {v.x, v.y};
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            if (DT == RMLX_BF16) {
+              f[4 * kk + 2 * e] = __uint_as_float(w[e] << 16);
+              f[4 * kk + 2 * e + 1] = __uint_as_float(w[e] & 0xffff0000u);
+            } else {
+              const float2 t2 = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
+              f[4 * kk + 2 * e] = t2.x;
+              f[4 * kk + 2 * e + 1] = t2.y;
+            }
+          }
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < NSEG; ++j) {
+          const uint4 v = hr < G ? __ldg(reinterpret_cast<const uint4*>(qrow + (32 * j + 8 * c) * 2)) : make_uint4(0u, 0u, 0u, 0u);
+          const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            if (DT == RMLX_BF16) {
+              f[8 * j + 2 * e] = __uint_as_float(w[e] << 16);
+              f[8 * j + 2 * e + 1] = __uint_as_float(w[e] & 0xffff0000u);
+            } else {
+              const float2 t2 = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
+              f[8 * j + 2 * e] = t2.x;
+              f[8 * j + 2 * e + 1] = t2.y;
+            }
+          }
+        }
+      }
+      float mx = 0.0f;
+#pragma unroll
+      for (int i = 0; i < NV; ++i) mx = fmaxf(mx, fabsf(f[i]));
+      mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, 2));
+      const float msc = mx > 0.0f ? mx : 1.0f, inv = __frcp_rn(msc);
+#pragma unroll
+      for (int i = 0; i < NV; ++i) f[i] = __half2float(__float2half_rn(f[i] * inv));
+      // fragments, and the group sums (a group holds whole k-steps)
+      float gsum = 0.0f;
+#pragma unroll
+      for (int kk = 0; kk < KT; ++kk) {
+        if (BITS == 8) {  // k-step kk: dims 16kk + 4c + (0, 1) | (2, 3)
+          qb[n][kk][0] = pack2<RMLX_F16>(f[4 * kk], f[4 * kk + 1]);
+          qb[n][kk][1] = pack2<RMLX_F16>(f[4 * kk + 2], f[4 * kk + 3]);
+          gsum += (f[4 * kk] + f[4 * kk + 1]) + (f[4 * kk + 2] + f[4 * kk + 3]);
+        } else {  // k-step 2j + u: dims 32j + 8c + (2u, 2u+4) | (2u+1, 2u+5)
+          const int j = kk >> 1, u = kk & 1;
+          qb[n][kk][0] = pack2<RMLX_F16>(f[8 * j + 2 * u], f[8 * j + 2 * u + 4]);
+          qb[n][kk][1] = pack2<RMLX_F16>(f[8 * j + 2 * u + 1], f[8 * j + 2 * u + 5]);
+          gsum += (f[8 * j + 2 * u] + f[8 * j + 2 * u + 4]) + (f[8 * j + 2 * u + 1] + f[8 * j + 2 * u + 5]);
+        }
+        if ((((kk + 1) << 4) & (gs - 1)) == 0) {  // the group ends with this k-step
+          gsum += __shfl_xor_sync(FULL, gsum, 1);
+          gsum += __shfl_xor_sync(FULL, gsum, 2);
+          if (c == 0) qgs[((kk << 4) >> gs_log2) * 16 + hr] = gsum;
+          gsum = 0.0f;
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 2; ++e) fsc[n][e] = __shfl_sync(FULL, msc, (2 * c + e) * 4) * scale_log2;
+    }
+    __syncwarp();
+
+    auto load_chunk = [&](int ci) {
+      const uint32_t dst = wbuf + (ci % STAGES) * STAGE;
+      const int tc = t_begin + ci * ATT_CHUNK;
+      if (!aligned_blocks) {
+        load_quant_chunk<NSEG>(dst, g, layer, h, btrow, tc, t_end, false, vdelta, lane, err);
+        return;
+      }
+      // the chunk's 16 code rows and 16 meta rows are each a contiguous run of the tile
+      const int32_t blk = __ldg(btrow + tc / g.bs);
+      const bool ok = blk >= 0 && blk < g.nblocks;
+      if (!ok && lane == 0) atomicOr(err, DEV_ERR_BLOCK);
+      const int nb = ok ? 16 : 0;
+      const uint8_t* tile = ok ? g.base + g.tile_off(blk, layer, 0, h) : g.base;
+      const int r0 = tc % g.bs;
+      const uint8_t* codes = tile + (int64_t)r0 * RB;
+#pragma unroll
+      for (int i = 0; i < CU; ++i) {
+        const int u = lane + 32 * i, row = u / NSEG, ch = u % NSEG;
+        const uint32_t so = row * RB + (code_col<NSEG>(row, ch) << 4);
+        const uint8_t* sp = ok ? codes + u * 16 : g.base;
+        cp_async16(dst + so, sp, nb);
+        cp_async16(dst + RAWH + so, ok ? sp + vdelta : g.base, nb);
+      }
+      const uint8_t* meta = tile + (int64_t)g.bs * RB + (int64_t)r0 * MB;
+      for (int x = lane; x < MB; x += 32) {  // 16 meta rows = MB 16-byte units
+        const uint8_t* sp = ok ? meta + x * 16 : g.base;
+        cp_async16(dst + ATT_CHUNK * RB + x * 16, sp, nb);
+        cp_async16(dst + RAWH + ATT_CHUNK * RB + x * 16, ok ? sp + vdelta : g.base, nb);
+      }
+      cp_async_commit();
+    };
+
+    float o[NH][MT][4];
+#pragma unroll
+    for (int n = 0; n < NH; ++n)
+#pragma unroll
+      for (int d = 0; d < MT; ++d) o[n][d][0] = o[n][d][1] = o[n][d][2] = o[n][d][3] = 0.0f;
+    float mrun[NH][2], lrun[NH][2];  // heads 8n + 2c + e: running max, this lane's share of the sum
+#pragma unroll
+    for (int n = 0; n < NH; ++n) mrun[n][0] = mrun[n][1] = -INFINITY, lrun[n][0] = lrun[n][1] = 0.0f;
+
+#pragma unroll
+    for (int ci = 0; ci < STAGES - 1; ++ci) {
+      if (ci < nchunks) load_chunk(ci);
+      else cp_async_commit();
+    }
+    for (int ci = 0; ci < nchunks; ++ci) {
+      if (ci + STAGES - 1 < nchunks) load_chunk(ci + STAGES - 1);
+      else cp_async_commit();
+      cp_async_wait<STAGES - 1>();
+      __syncwarp();
+      const uint32_t kraw = wbuf + (ci % STAGES) * STAGE, vraw = kraw + RAWH;
+      const uint32_t kmeta = kraw + ATT_CHUNK * RB, vmeta = vraw + ATT_CHUNK * RB;
+      const int nval = min(ATT_CHUNK, t_end - t_begin - ci * ATT_CHUNK);
+      const bool val0 = r < nval, val1 = r + 8 < nval;  // this lane's tokens r and r + 8
+      // (scale, centred zero) of group gi for tokens r and r + 8; zeros past the end
+      auto load_meta = [&](uint32_t mbase, int gi, float& s0, float& z0, float& s1, float& z1) {
+        float a[2], b[2];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          const uint32_t ad = mbase + (r + 8 * k) * MB;
+          if (MF32) {
+            const uint2 m = lds64(ad + gi * 8);
+            a[k] = __uint_as_float(m.x);
+            b[k] = __uint_as_float(m.y);
+          } else {
+            const uint32_t m = lds32(ad + gi * 4);
+            const float2 fm = __half22float2(*reinterpret_cast<const __half2*>(&m));
+            a[k] = fm.x;
+            b[k] = fm.y;
+          }
+        }
+        constexpr float OFF = (float)(1 << (BITS - 1));
+        s0 = val0 ? a[0] : 0.0f;
+        z0 = val0 ? fmaf(a[0], OFF, b[0]) : 0.0f;
+        s1 = val1 ? a[1] : 0.0f;
+        z1 = val1 ? fmaf(a[1], OFF, b[1]) : 0.0f;
+      };
+
+      // S^T = K Q^T, folded into sacc at the end of each group
+      float sacc[NH][4], sgp[NH][4];
+#pragma unroll
+      for (int n = 0; n < NH; ++n)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) sacc[n][k] = sgp[n][k] = 0.0f;
+#pragma unroll
+      for (int sc2 = 0; sc2 < NSEG; sc2 += 2) {
+        uint32_t wv[4];  // tokens 0-7 | 8-15 of column sc2, then of column sc2 + 1
+        ldsm_x4(kraw + trow * RB + (code_col<NSEG>(trow, sc2 + (mi >> 1)) << 4), wv[0], wv[1], wv[2], wv[3]);
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          const uint32_t lo = wv[2 * half], hi = wv[2 * half + 1];  // tokens r, r + 8
+          uint32_t a[MPS][4];
+          if (BITS == 8) {
+            a[0][0] = codes8(lo, 0x4140u);
+            a[0][1] = codes8(hi, 0x4140u);
+            a[0][2] = codes8(lo, 0x4342u);
+            a[0][3] = codes8(hi, 0x4342u);
+          } else {
+            uint32_t pl[4], ph[4];
+            codes4(lo, pl);
+            codes4(hi, ph);
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              a[u][0] = pl[2 * u];
+              a[u][1] = ph[2 * u];
+              a[u][2] = pl[2 * u + 1];
+              a[u][3] = ph[2 * u + 1];
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < MPS; ++u) {
+            const int kk = (sc2 + half) * MPS + u;
+#pragma unroll
+            for (int n = 0; n < NH; ++n) mma16816<RMLX_F16>(sgp[n], a[u], qb[n][kk][0], qb[n][kk][1]);
+            if ((((kk + 1) << 4) & (gs - 1)) == 0) {  // the group ends with this k-step
+              const int gi = (kk << 4) >> gs_log2;
+              float s0, z0, s1, z1;
+              load_meta(kmeta, gi, s0, z0, s1, z1);
+#pragma unroll
+              for (int n = 0; n < NH; ++n) {
+                const float2 qs = *reinterpret_cast<const float2*>(qgs + gi * 16 + 8 * n + 2 * c);
+                sacc[n][0] = fmaf(s0, sgp[n][0], fmaf(z0, qs.x, sacc[n][0]));
+                sacc[n][1] = fmaf(s0, sgp[n][1], fmaf(z0, qs.y, sacc[n][1]));
+                sacc[n][2] = fmaf(s1, sgp[n][2], fmaf(z1, qs.x, sacc[n][2]));
+                sacc[n][3] = fmaf(s1, sgp[n][3], fmaf(z1, qs.y, sacc[n][3]));
+#pragma unroll
+                for (int k = 0; k < 4; ++k) sgp[n][k] = 0.0f;
+              }
+            }
+          }
+        }
+      }
+      // online softmax (log2 domain) per head over the chunk's tokens
+      bool rescale = false;
+      float al[NH][2];
+#pragma unroll
+      for (int n = 0; n < NH; ++n)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float x0 = val0 ? sacc[n][e] * fsc[n][e] : -INFINITY;
+          const float x1 = val1 ? sacc[n][2 + e] * fsc[n][e] : -INFINITY;
+          float mx = fmaxf(x0, x1);
+          mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, 4));
+          mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, 8));
+          mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, 16));
+          const float nm = fmaxf(mrun[n][e], mx);  // finite: every chunk has a valid token
+          al[n][e] = ex2(mrun[n][e] - nm);
+          mrun[n][e] = nm;
+          sacc[n][e] = ex2(x0 - nm);
+          sacc[n][2 + e] = ex2(x1 - nm);
+          lrun[n][e] = lrun[n][e] * al[n][e] + (sacc[n][e] + sacc[n][2 + e]);
+          rescale |= al[n][e] != 1.0f;
+        }
+      if (__any_sync(FULL, rescale)) {
+#pragma unroll
+        for (int n = 0; n < NH; ++n)
+#pragma unroll
+          for (int d = 0; d < MT; ++d) {
+            o[n][d][0] *= al[n][0];
+            o[n][d][1] *= al[n][1];
+            o[n][d][2] *= al[n][0];
+            o[n][d][3] *= al[n][1];
+          }
+      }
+
+      // O^T += V^T P^T, one group at a time
+      uint32_t pb[NH][2];
+      float cz[NH][2], smx = 1.0f;
+#pragma unroll
+      for (int sc2 = 0; sc2 < NSEG; sc2 += 2) {
+        uint32_t wv[4];  // tokens (2c, 2c+1) | (8+2c, 9+2c) of column sc2, then of column sc2 + 1
+        ldsm_x4_t(vraw + trow * RB + (code_col<NSEG>(trow, sc2 + (mi >> 1)) << 4), wv[0], wv[1], wv[2], wv[3]);
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          const int col = sc2 + half;
+          if (((col * SEGD) & (gs - 1)) == 0) {  // the column starts a group
+            const int gi = (col * SEGD) >> gs_log2;
+            float s0, z0, s1, z1;
+            load_meta(vmeta, gi, s0, z0, s1, z1);
+            float am = fmaxf(fabsf(s0), fabsf(s1));
+            am = fmaxf(am, __shfl_xor_sync(FULL, am, 4));
+            am = fmaxf(am, __shfl_xor_sync(FULL, am, 8));
+            am = fmaxf(am, __shfl_xor_sync(FULL, am, 16));
+            smx = am > 0.0f ? am : 1.0f;
+            const float inv = __frcp_rn(smx), a0 = s0 * inv, a1 = s1 * inv;
+#pragma unroll
+            for (int n = 0; n < NH; ++n) {
+              pb[n][0] = movmatrix_t(pack2<RMLX_F16>(sacc[n][0] * a0, sacc[n][1] * a0));
+              pb[n][1] = movmatrix_t(pack2<RMLX_F16>(sacc[n][2] * a1, sacc[n][3] * a1));
+#pragma unroll
+              for (int e = 0; e < 2; ++e) {
+                float zs = fmaf(sacc[n][e], z0, sacc[n][2 + e] * z1);
+                zs += __shfl_xor_sync(FULL, zs, 4);
+                zs += __shfl_xor_sync(FULL, zs, 8);
+                zs += __shfl_xor_sync(FULL, zs, 16);
+                cz[n][e] = zs * inv;
+              }
+            }
+          }
+          const uint32_t lo = wv[2 * half], hi = wv[2 * half + 1];
+          uint32_t a[MPS][4];
+          if (BITS == 8) {  // rows r, r + 8: dims 2r, 2r + 1 of the column
+            a[0][0] = codes8(lo, 0x4240u);
+            a[0][1] = codes8(lo, 0x4341u);
+            a[0][2] = codes8(hi, 0x4240u);
+            a[0][3] = codes8(hi, 0x4341u);
+          } else {  // m-tile u, rows r, r + 8: dims 4r + 2u, 4r + 2u + 1 of the column
+            uint32_t pl[4], ph[4];
+            codes4(lo, pl);
+            codes4(hi, ph);
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              a[u][0] = pl[2 * u];
+              a[u][1] = pl[2 * u + 1];
+              a[u][2] = ph[2 * u];
+              a[u][3] = ph[2 * u + 1];
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < MPS; ++u)
+#pragma unroll
+            for (int n = 0; n < NH; ++n) {
+              float t[4];
+              mma16816_c(t, a[u], pb[n][0], pb[n][1], cz[n][0], cz[n][1], cz[n][0], cz[n][1]);
+              float* od = o[n][col * MPS + u];
+              od[0] = fmaf(smx, t[0], od[0]);
+              od[1] = fmaf(smx, t[1], od[1]);
+              od[2] = fmaf(smx, t[2], od[2]);
+              od[3] = fmaf(smx, t[3], od[3]);
+            }
+        }
+      }
+      __syncwarp();  // the stage is overwritten by the next load
+    }
+    cp_async_wait<0>();
+    __syncwarp();
+
+    // m-tile col * MPS + u, rows r and r + 8 hold dimensions
+    // col * SEGD + 2 MPS r + 2u and + 1; elements e, 2 + e head 8n + 2c + e
+    const int nsp = cub[s + 1] - cub[s];
+#pragma unroll
+    for (int n = 0; n < NH; ++n)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        float lt = lrun[n][e];
+        lt += __shfl_xor_sync(FULL, lt, 4);
+        lt += __shfl_xor_sync(FULL, lt, 8);
+        lt += __shfl_xor_sync(FULL, lt, 16);
+        const int hq = 8 * n + 2 * c + e;  // query head within the group
+        if (hq >= G) continue;
+        if (nsp == 1) {
+          const float il = 1.0f / lt;
+          uint8_t* ob = out + ((int64_t)s * qheads + (int64_t)h * G + hq) * ROWB;
+#pragma unroll
+          for (int col = 0; col < NSEG; ++col) {
+            const int d0 = col * SEGD + 2 * MPS * r;
+            uint32_t w[MPS];
+#pragma unroll
+            for (int u = 0; u < MPS; ++u)
+              w[u] = pack2<DT>(o[n][col * MPS + u][e] * il, o[n][col * MPS + u][2 + e] * il);
+            if constexpr (MPS == 1) *reinterpret_cast<uint32_t*>(ob + d0 * 2) = w[0];
+            else *reinterpret_cast<uint2*>(ob + d0 * 2) = make_uint2(w[0], w[1]);
+          }
+        } else {
+          float* po = part_o + (it * (int64_t)G + hq) * HD;
+#pragma unroll
+          for (int col = 0; col < NSEG; ++col) {
+            const int d0 = col * SEGD + 2 * MPS * r;
+            if constexpr (MPS == 1) {
+              *reinterpret_cast<float2*>(po + d0) = make_float2(o[n][col][e], o[n][col][2 + e]);
+            } else {
+              *reinterpret_cast<float4*>(po + d0) = make_float4(o[n][2 * col][e], o[n][2 * col][2 + e],
+                                                                o[n][2 * col + 1][e], o[n][2 * col + 1][2 + e]);
+            }
+          }
+          if (r == 0) *reinterpret_cast<float2*>(part_ml + it * (int64_t)2 * G + 2 * hq) = make_float2(mrun[n][e], lt);
+        }
+      }
+  }
+}
+
 // One warp per (sequence, query head) of the sequences held by two or more
 // splits (the split kernel wrote the others): combine_splits.
 template <int DT, int HD>
@@ -698,6 +1241,53 @@ AttnFn attn_kernel_of(const rmlx_pool_config& c) {
   return c.head_dim == 128 ? (bf ? pick_attn<RMLX_BF16, 128>(bits, mf32) : pick_attn<RMLX_F16, 128>(bits, mf32))
                            : (bf ? pick_attn<RMLX_BF16, 64>(bits, mf32) : pick_attn<RMLX_F16, 64>(bits, mf32));
 }
+
+// Quantised pools whose groups span whole k-steps and code columns are read
+// as codes (paged_decode_attn_codes_kernel); the others are dequantised into
+// a tile.
+constexpr int CQ_STAGES = 2;
+constexpr int cq_minb(int nh) { return nh == 1 ? 4 : 2; }  // CTAs per SM the register budget allows
+bool reads_codes(const rmlx_pool_config& c) {
+  return (c.quant_bits == 8 && c.group_size >= 16) || (c.quant_bits == 4 && c.group_size >= 32);
+}
+
+size_t attn_codes_smem(int nseq, int stages, int row_bytes, int meta_row_bytes) {
+  const size_t scan_bytes = ((size_t)2 * (nseq + 1) * 4 + 127) & ~(size_t)127;
+  const size_t stage = 2 * ATT_CHUNK * (size_t)(row_bytes + meta_row_bytes);
+  return scan_bytes + (size_t)ATT_WARPS * (stages * stage + CQ_QS_BYTES);
+}
+
+template <int DT, int HD, int NH>
+AttnFn pick_codes(int bits, bool mf32) {
+  constexpr int MINB = cq_minb(NH);
+  if (bits == 8) return mf32 ? paged_decode_attn_codes_kernel<DT, HD, 8, true, NH, CQ_STAGES, MINB>
+                             : paged_decode_attn_codes_kernel<DT, HD, 8, false, NH, CQ_STAGES, MINB>;
+  return mf32 ? paged_decode_attn_codes_kernel<DT, HD, 4, true, NH, CQ_STAGES, MINB>
+              : paged_decode_attn_codes_kernel<DT, HD, 4, false, NH, CQ_STAGES, MINB>;
+}
+template <int HD, int NH>
+AttnFn pick_codes(const rmlx_pool_config& c) {
+  const bool mf32 = c.meta_dtype == RMLX_F32;
+  return c.dtype == RMLX_BF16 ? pick_codes<RMLX_BF16, HD, NH>(c.quant_bits, mf32)
+                              : pick_codes<RMLX_F16, HD, NH>(c.quant_bits, mf32);
+}
+
+// The split kernel a pool's launches use and its dynamic shared memory.
+struct AttnPlan {
+  AttnFn fn;
+  size_t smem;
+};
+AttnPlan attn_plan(const rmlx_kv_pool* p, int nseq, int G) {
+  const rmlx_pool_config& c = p->cfg;
+  const int hd = c.head_dim;
+  if (reads_codes(c)) {
+    AttnFn fn = hd == 128 ? (G <= 8 ? pick_codes<128, 1>(c) : pick_codes<128, 2>(c))
+                          : (G <= 8 ? pick_codes<64, 1>(c) : pick_codes<64, 2>(c));
+    return {fn, attn_codes_smem(nseq, CQ_STAGES, (int)p->row_bytes, (int)p->meta_row_bytes)};
+  }
+  return {attn_kernel_of(c), attn_smem(nseq, hd, ATT_STAGES, ATT_QSMEM, c.quant_bits, (int)p->row_bytes,
+                                       (int)p->meta_row_bytes)};
+}
 }  // namespace
 
 extern "C" {
@@ -712,12 +1302,10 @@ rmlx_status rmlx_kv_attention_workspace_size(const rmlx_kv_pool* p, int32_t q_he
   if ((c.dtype == RMLX_F16 || c.dtype == RMLX_BF16) && (c.head_dim == 64 || c.head_dim == 128)) {
     // room for the smaller splits a launch with few work items takes (down
     // to 64 tokens: at most 4x the splits of a launch below the target)
-    AttnFn fa = attn_kernel_of(c);
-    const size_t smem = attn_smem(num_seqs, c.head_dim, ATT_STAGES, ATT_QSMEM, c.quant_bits, (int)p->row_bytes,
-                                  (int)p->meta_row_bytes);
+    const AttnPlan plan = attn_plan(p, num_seqs, q_heads_per_kv);
     DeviceGuard dg(p->device);
-    if (smem <= 227 * 1024 && prepare_smem(fa, smem) == RMLX_OK) {
-      const int64_t target = attn_target(fa, smem, p->num_sms);
+    if (plan.smem <= 227 * 1024 && prepare_smem(plan.fn, plan.smem) == RMLX_OK) {
+      const int64_t target = attn_target(plan.fn, plan.smem, p->num_sms);
       splits = std::max<int64_t>(splits, 4 * ((target + c.num_kv_heads - 1) / c.num_kv_heads) + num_seqs);
     }
   }
@@ -754,7 +1342,8 @@ rmlx_status rmlx_kv_decode_attention(rmlx_kv_pool* p, int32_t layer, const void*
   cudaStream_t st = (cudaStream_t)stream;
   const bool bf = c.dtype == RMLX_BF16;
   const int bits = c.quant_bits;
-  AttnFn fa = attn_kernel_of(c);
+  const AttnPlan plan = attn_plan(p, num_seqs, G);
+  AttnFn fa = plan.fn;
   CombineFn fc = hd == 128 ? (bf ? attn_combine_kernel<RMLX_BF16, 128> : attn_combine_kernel<RMLX_F16, 128>)
                            : (bf ? attn_combine_kernel<RMLX_BF16, 64> : attn_combine_kernel<RMLX_F16, 64>);
   if (!p->attn_work) {  // the item counter: pool memory, zero between launches
@@ -765,7 +1354,7 @@ rmlx_status rmlx_kv_decode_attention(rmlx_kv_pool* p, int32_t layer, const void*
     }
     p->attn_work = static_cast<unsigned long long*>(w);
   }
-  const size_t smem = attn_smem(num_seqs, hd, ATT_STAGES, ATT_QSMEM, bits, (int)p->row_bytes, (int)p->meta_row_bytes);
+  const size_t smem = plan.smem;
   if (smem > 227 * 1024) return fail(RMLX_E_BAD_ARG, "num_seqs too large for one decode attention launch");
   rmlx_status s;
   if ((s = prepare_smem(fa, smem)) != RMLX_OK) return s;

@@ -9,6 +9,14 @@ before P V (relative error 2^-9 for bf16, 2^-12 for f16 per weight), and the
 output is rounded to the pool's type.  With |V| <~ 4.5 that bounds the
 error by about 4 * 2^-9 * 4.5 = 0.035 (bf16) and 0.005 (f16); the tests use
 max-abs 0.03 / 0.004 and an RMS bound ten times tighter.
+
+Quantised pools with group_size >= 16 (8-bit) or >= 32 (4-bit) are read as
+codes: the queries are rounded to f16 after division by their row's max
+|q| (2^-12), the products of codes and queries are exact, and the weights
+P s / smax are rounded to f16 (2^-12) instead of P to the pool's type; the
+dequantised rows themselves are never rounded, while the reference reads
+them rounded to the pool's type (2^-9 for bf16, 2^-12 for f16).  The same
+bounds hold.
 """
 import numpy as np
 import pytest
@@ -202,6 +210,14 @@ def test_quantised_block_sizes_and_groups(cuda, bs, D, gs, dt):
     N = 700 // bs + 40
     for bits in (8, 4):
         run_attn_quant(cuda, 1, 2, D, bs, N, dt, 8, [3, 16, 31, 300], 80 + bs + bits, bits, gs, orc.F16)
+
+
+@pytest.mark.parametrize("G", [1, 12, 16])
+def test_quantised_query_groups(cuda, G):
+    """One query head per KV head, and 12 or 16 (two 8-wide head tiles in
+    the kernel that reads codes)."""
+    for bits in (8, 4):
+        run_attn_quant(cuda, 1, 4, 128, 16, 200, orc.BF16, G, [5, 77, 300, 0], 90 + G + bits, bits, 64, orc.F16)
 
 
 def test_bad_arguments(cuda):
