@@ -660,14 +660,21 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
 // heads the N columns (G <= 8: one 8-wide n-tile; up to 16: two), so a
 // 16-token chunk costs one MMA per k-step instead of two:
 //   S^T = K Q^T:  S^T[t][j] = sum over groups g of
-//                 s_tg (C_tg . q'_jg) + z_tg (sum of q'_jg),
+//                 s_tg (c_tg . q'_jg) + z_tg (sum of q'_jg),
 //   O^T += V^T P^T:  O^T[d][j] += smax_g ((C_g^T (P^T o s_g / smax_g))[d][j]
 //                                  + (sum_t P[j][t] z_tg) / smax_g)
 // with q' = q / max|q| of its row in f16 (the factor returns in the softmax
 // scale) and smax_g the chunk's largest |s_tg| (the f16 weights P s / smax
-// stay in [-1, 1] whatever the scales).  Codes enter centred (code -
-// 2^(bits-1), exact f16 integers) and the zeros as z + 2^(bits-1) s, which
-// halves the magnitude of s * code and with it the weights' rounding.
+// stay in [-1, 1] whatever the scales).
+//
+// A code enters as the f16 that a byte permute (or a mask) makes of it
+// directly: 1024 + code (8-bit; 4-bit low nibbles) or 64 + code (4-bit high
+// nibbles, in place: ulp 1/16).  The offsets are taken out in f32 through the
+// zero terms: per group, S^T gets - s (1024 sum of q' over the dims riding on
+// 1024 + 64 sum over those riding on 64), and O^T's accumulator starts at
+// sum_t P z / smax - (offset + 2^(bits-1)) sum_t P s / smax, with the weights
+// P s / smax summed as rounded, so that the products see centred codes
+// (code - 2^(bits-1)) and the zeros z + 2^(bits-1) s.
 //
 // Fragments come straight from the staged code rows (16-byte columns
 // XOR-swizzled, read with ldmatrix):
@@ -684,33 +691,21 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
 //     token, packed to f16 and transposed in registers (movmatrix) into the
 //     B fragments (tokens 2c, 2c+1, head r).
 // A group spans whole k-steps and whole code columns, hence the floor on
-// the group size.
+// the group size; the group size is a template parameter, so every
+// group boundary and meta offset is known at compile time.
 
-// Two code bytes of w (selector 0x4j4i: bytes i, j) as centred f16
-// integers: 1024 + code is an f16 whose low mantissa byte is the code;
-// 1152 = 1024 + 128 is subtracted.
-__device__ __forceinline__ uint32_t codes8(uint32_t w, uint32_t sel) {
-  const uint32_t x = __byte_perm(w, 0x64646464u, sel);
-  __half2 h = *reinterpret_cast<const __half2*>(&x);
-  const __half2 m = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));
-  h = __hsub2(h, m);
-  return *reinterpret_cast<const uint32_t*>(&h);
-}
-// Eight 4-bit codes of w as four centred f16x2 pairs: low nibbles of bytes
-// 0 and 2, high nibbles of bytes 0 and 2, then the same of bytes 1 and 3.
-// A low nibble rides on 1024 (ulp 1), a high nibble, in place, on 64 (ulp
-// 1/16); 1032 and 72 are subtracted.
+// Two code bytes of w (selector 0x4j4i: bytes i, j) as the f16 pair
+// (1024 + code_i, 1024 + code_j).
+__device__ __forceinline__ uint32_t codes8(uint32_t w, uint32_t sel) { return __byte_perm(w, 0x64646464u, sel); }
+// Eight 4-bit codes of w as four f16 pairs: low nibbles of bytes 0 and 2
+// (1024 + n), high nibbles of bytes 0 and 2 (64 + n), then the same of
+// bytes 1 and 3.
 __device__ __forceinline__ void codes4(uint32_t w, uint32_t (&p)[4]) {
-  const __half2 lo = __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408));
-  const __half2 hi = __halves2half2(__ushort_as_half(0x5480), __ushort_as_half(0x5480));
   const uint32_t w8 = w >> 8;
-  const uint32_t x[4] = {(w & 0x000F000Fu) | 0x64006400u, (w & 0x00F000F0u) | 0x54005400u,
-                         (w8 & 0x000F000Fu) | 0x64006400u, (w8 & 0x00F000F0u) | 0x54005400u};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const __half2 h = __hsub2(*reinterpret_cast<const __half2*>(&x[i]), (i & 1) ? hi : lo);
-    p[i] = *reinterpret_cast<const uint32_t*>(&h);
-  }
+  p[0] = (w & 0x000F000Fu) | 0x64006400u;
+  p[1] = (w & 0x00F000F0u) | 0x54005400u;
+  p[2] = (w8 & 0x000F000Fu) | 0x64006400u;
+  p[3] = (w8 & 0x00F000F0u) | 0x54005400u;
 }
 
 // An 8x8 matrix of 16-bit elements held as ldmatrix holds it (lane 4i + j:
@@ -730,9 +725,18 @@ __device__ __forceinline__ void mma16816_c(float* d, const uint32_t* a, uint32_t
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(c0), "f"(c1), "f"(c2), "f"(c3));
 }
 
-constexpr int CQ_QS_BYTES = 512;  // per warp: sums of the queries per (group, head), 8 x 16 f32
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
-template <int DT, int HD, int BITS, bool MF32, int NH, int STAGES, int MINB>
+// Per warp: per (group, head) the sums of the queries' f16 values over the
+// group's dims riding on 1024 (x) and on 64 (y; 4-bit high nibbles).
+constexpr int CQ_QS_BYTES = 8 * 16 * 8;
+constexpr int CQ_STAGES = 2;  // chunks in flight per warp
+
+template <int HD, int BITS, int GS, int NH, int MINB>
 __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
     paged_decode_attn_codes_kernel(PoolGeo g, int layer, const uint8_t* __restrict__ q, int G,
                                    const int32_t* __restrict__ bt, int bt_stride, const int32_t* __restrict__ lens,
@@ -747,22 +751,26 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
   constexpr int KT = HD / 16;              // k-steps of S^T
   constexpr int MPS = BITS == 8 ? 1 : 2;   // m-tiles of O^T (16 dims) per code column; k-steps per column
   constexpr int MT = NSEG * MPS;           // m-tiles of O^T
+  constexpr int NG = HD / GS;              // groups per row
   constexpr int CU = ATT_CHUNK * NSEG / 32;  // 16-byte code units per lane per chunk, K or V
+  constexpr float OFF = (float)(1 << (BITS - 1));  // centring of the codes
   constexpr unsigned FULL = 0xffffffffu;
   static_assert(NSEG % 2 == 0 && CU >= 1 && (BITS == 8 || BITS == 4) && (NH == 1 || NH == 2), "shape");
+  static_assert(GS >= 16 * MPS && GS <= HD && NG <= 8, "a group spans whole k-steps and code columns");
   const int MB = g.meta_row_bytes;
+  const bool mf32 = MB == NG * 8;          // f32 (scale, zero) pairs, else f16
+  const bool bf = g.dtype == RMLX_BF16;
   const int RAWH = ATT_CHUNK * (RB + MB);  // K (or V) part of a stage
   const int STAGE = 2 * RAWH;
-  const int gs = 1 << gs_log2;
   extern __shared__ __align__(128) uint8_t smem[];
   int32_t* cub = reinterpret_cast<int32_t*>(smem);
   int32_t* cut = cub + nseq + 1;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const size_t scan_bytes = ((size_t)2 * (nseq + 1) * 4 + 127) & ~(size_t)127;
-  const int WBYTES = STAGES * STAGE + CQ_QS_BYTES;
+  const int WBYTES = CQ_STAGES * STAGE + CQ_QS_BYTES;
   uint8_t* wgen = smem + scan_bytes + (size_t)warp * WBYTES;
   const uint32_t wbuf = (uint32_t)__cvta_generic_to_shared(wgen);
-  float* qgs = reinterpret_cast<float*>(wgen + STAGES * STAGE);  // [group][head]
+  float2* qgs = reinterpret_cast<float2*>(wgen + CQ_STAGES * STAGE);  // [group][head]
   pdl_wait();
   pdl_release();
   const int split = pick_split(lens, nseq, g.heads, target, cap_splits, cub, cut);
@@ -807,40 +815,34 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
       const int hr = 8 * n + r;
       const uint8_t* qrow = q + ((int64_t)s * qheads + (int64_t)h * G + hr) * ROWB;
       constexpr int NV = HD / 4;  // dimensions per lane: 8-bit 16kk + 4c + (0..3); 4-bit 32j + 8c + (0..7)
+      constexpr int VW = BITS == 8 ? 2 : 4;  // 32-bit words per load
       float f[NV];
-      if (BITS == 8) {
 #pragma unroll
-        for (int kk = 0; kk < KT; ++kk) {
-          const uint2 v = hr < G ? __ldg(reinterpret_cast<const uint2*>(qrow + (16 * kk + 4 * c) * 2)) : make_uint2(0u, 0u);
-          const uint32_t w[2] = {v.x, v.y};
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            if (DT == RMLX_BF16) {
-              f[4 * kk + 2 * e] = __uint_as_float(w[e] << 16);
-              f[4 * kk + 2 * e + 1] = __uint_as_float(w[e] & 0xffff0000u);
-            } else {
-              const float2 t2 = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
-              f[4 * kk + 2 * e] = t2.x;
-              f[4 * kk + 2 * e + 1] = t2.y;
-            }
-          }
+      for (int j = 0; j < NV / (2 * VW); ++j) {
+        uint32_t w[VW];
+        const uint8_t* src = qrow + (BITS == 8 ? (16 * j + 4 * c) : (32 * j + 8 * c)) * 2;
+        if (BITS == 8) {
+          const uint2 v = hr < G ? __ldg(reinterpret_cast<const uint2*>(src)) : make_uint2(0u, 0u);
+          w[0] = v.x;
+          w[1] = v.y;
+        } else {
+          const uint4 v = hr < G ? __ldg(reinterpret_cast<const uint4*>(src)) : make_uint4(0u, 0u, 0u, 0u);
+          w[0] = v.x;
+          w[1] = v.y;
+          w[2 % VW] = v.z;
+          w[3 % VW] = v.w;
         }
-      } else {
 #pragma unroll
-        for (int j = 0; j < NSEG; ++j) {
-          const uint4 v = hr < G ? __ldg(reinterpret_cast<const uint4*>(qrow + (32 * j + 8 * c) * 2)) : make_uint4(0u, 0u, 0u, 0u);
-          const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            if (DT == RMLX_BF16) {
-              f[8 * j + 2 * e] = __uint_as_float(w[e] << 16);
-              f[8 * j + 2 * e + 1] = __uint_as_float(w[e] & 0xffff0000u);
-            } else {
-              const float2 t2 = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
-              f[8 * j + 2 * e] = t2.x;
-              f[8 * j + 2 * e + 1] = t2.y;
-            }
+        for (int e = 0; e < VW; ++e) {
+          float2 t2;
+          if (bf) {
+            t2.x = __uint_as_float(w[e] << 16);
+            t2.y = __uint_as_float(w[e] & 0xffff0000u);
+          } else {
+            t2 = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
           }
+          f[2 * VW * j + 2 * e] = t2.x;
+          f[2 * VW * j + 2 * e + 1] = t2.y;
         }
       }
       float mx = 0.0f;
@@ -848,28 +850,41 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
       for (int i = 0; i < NV; ++i) mx = fmaxf(mx, fabsf(f[i]));
       mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, 1));
       mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, 2));
-      const float msc = mx > 0.0f ? mx : 1.0f, inv = __frcp_rn(msc);
+      const float msc = mx > 0.0f ? mx : 1.0f, inv = rcp_approx(msc);
 #pragma unroll
       for (int i = 0; i < NV; ++i) f[i] = __half2float(__float2half_rn(f[i] * inv));
       // fragments, and the group sums (a group holds whole k-steps)
-      float gsum = 0.0f;
+      float gx = 0.0f, gy = 0.0f;
 #pragma unroll
       for (int kk = 0; kk < KT; ++kk) {
+        float p[4];  // the fragment's values: k positions 2c, 2c+1, 2c+8, 2c+9
         if (BITS == 8) {  // k-step kk: dims 16kk + 4c + (0, 1) | (2, 3)
-          qb[n][kk][0] = pack2<RMLX_F16>(f[4 * kk], f[4 * kk + 1]);
-          qb[n][kk][1] = pack2<RMLX_F16>(f[4 * kk + 2], f[4 * kk + 3]);
-          gsum += (f[4 * kk] + f[4 * kk + 1]) + (f[4 * kk + 2] + f[4 * kk + 3]);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) p[i] = f[4 * kk + i];
         } else {  // k-step 2j + u: dims 32j + 8c + (2u, 2u+4) | (2u+1, 2u+5)
           const int j = kk >> 1, u = kk & 1;
-          qb[n][kk][0] = pack2<RMLX_F16>(f[8 * j + 2 * u], f[8 * j + 2 * u + 4]);
-          qb[n][kk][1] = pack2<RMLX_F16>(f[8 * j + 2 * u + 1], f[8 * j + 2 * u + 5]);
-          gsum += (f[8 * j + 2 * u] + f[8 * j + 2 * u + 4]) + (f[8 * j + 2 * u + 1] + f[8 * j + 2 * u + 5]);
+          p[0] = f[8 * j + 2 * u];
+          p[1] = f[8 * j + 2 * u + 4];
+          p[2] = f[8 * j + 2 * u + 1];
+          p[3] = f[8 * j + 2 * u + 5];
         }
-        if ((((kk + 1) << 4) & (gs - 1)) == 0) {  // the group ends with this k-step
-          gsum += __shfl_xor_sync(FULL, gsum, 1);
-          gsum += __shfl_xor_sync(FULL, gsum, 2);
-          if (c == 0) qgs[((kk << 4) >> gs_log2) * 16 + hr] = gsum;
-          gsum = 0.0f;
+        qb[n][kk][0] = pack2<RMLX_F16>(p[0], p[1]);
+        qb[n][kk][1] = pack2<RMLX_F16>(p[2], p[3]);
+        if (BITS == 8) {
+          gx += (p[0] + p[1]) + (p[2] + p[3]);
+        } else {  // positions 2c, 2c+1: low nibbles (on 1024); 2c+8, 2c+9: high nibbles (on 64)
+          gx += p[0] + p[1];
+          gy += p[2] + p[3];
+        }
+        if (((kk + 1) * 16) % GS == 0) {  // the group ends with this k-step
+          gx += __shfl_xor_sync(FULL, gx, 1);
+          gx += __shfl_xor_sync(FULL, gx, 2);
+          if (BITS == 4) {
+            gy += __shfl_xor_sync(FULL, gy, 1);
+            gy += __shfl_xor_sync(FULL, gy, 2);
+          }
+          if (c == 0) qgs[(kk * 16 / GS) * 16 + hr] = make_float2(gx, gy);
+          gx = gy = 0.0f;
         }
       }
 #pragma unroll
@@ -877,21 +892,25 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
     }
     __syncwarp();
 
+    // chunks are loaded in order: the block table entry and row of the next one
+    int ld_blk = 0, ld_row = 0;
+    if (aligned_blocks) {
+      ld_blk = t_begin / g.bs;
+      ld_row = t_begin - ld_blk * g.bs;
+    }
     auto load_chunk = [&](int ci) {
-      const uint32_t dst = wbuf + (ci % STAGES) * STAGE;
-      const int tc = t_begin + ci * ATT_CHUNK;
+      const uint32_t dst = wbuf + (ci % CQ_STAGES) * STAGE;
       if (!aligned_blocks) {
-        load_quant_chunk<NSEG>(dst, g, layer, h, btrow, tc, t_end, false, vdelta, lane, err);
+        load_quant_chunk<NSEG>(dst, g, layer, h, btrow, t_begin + ci * ATT_CHUNK, t_end, false, vdelta, lane, err);
         return;
       }
       // the chunk's 16 code rows and 16 meta rows are each a contiguous run of the tile
-      const int32_t blk = __ldg(btrow + tc / g.bs);
+      const int32_t blk = __ldg(btrow + ld_blk);
       const bool ok = blk >= 0 && blk < g.nblocks;
       if (!ok && lane == 0) atomicOr(err, DEV_ERR_BLOCK);
       const int nb = ok ? 16 : 0;
       const uint8_t* tile = ok ? g.base + g.tile_off(blk, layer, 0, h) : g.base;
-      const int r0 = tc % g.bs;
-      const uint8_t* codes = tile + (int64_t)r0 * RB;
+      const uint8_t* codes = tile + ld_row * RB;
 #pragma unroll
       for (int i = 0; i < CU; ++i) {
         const int u = lane + 32 * i, row = u / NSEG, ch = u % NSEG;
@@ -900,13 +919,18 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
         cp_async16(dst + so, sp, nb);
         cp_async16(dst + RAWH + so, ok ? sp + vdelta : g.base, nb);
       }
-      const uint8_t* meta = tile + (int64_t)g.bs * RB + (int64_t)r0 * MB;
+      const uint8_t* meta = tile + (int64_t)g.bs * RB + ld_row * MB;
       for (int x = lane; x < MB; x += 32) {  // 16 meta rows = MB 16-byte units
         const uint8_t* sp = ok ? meta + x * 16 : g.base;
         cp_async16(dst + ATT_CHUNK * RB + x * 16, sp, nb);
         cp_async16(dst + RAWH + ATT_CHUNK * RB + x * 16, ok ? sp + vdelta : g.base, nb);
       }
       cp_async_commit();
+      ld_row += ATT_CHUNK;
+      if (ld_row == g.bs) {
+        ld_row = 0;
+        ++ld_blk;
+      }
     };
 
     float o[NH][MT][4];
@@ -919,26 +943,26 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
     for (int n = 0; n < NH; ++n) mrun[n][0] = mrun[n][1] = -INFINITY, lrun[n][0] = lrun[n][1] = 0.0f;
 
 #pragma unroll
-    for (int ci = 0; ci < STAGES - 1; ++ci) {
+    for (int ci = 0; ci < CQ_STAGES - 1; ++ci) {
       if (ci < nchunks) load_chunk(ci);
       else cp_async_commit();
     }
     for (int ci = 0; ci < nchunks; ++ci) {
-      if (ci + STAGES - 1 < nchunks) load_chunk(ci + STAGES - 1);
+      if (ci + CQ_STAGES - 1 < nchunks) load_chunk(ci + CQ_STAGES - 1);
       else cp_async_commit();
-      cp_async_wait<STAGES - 1>();
+      cp_async_wait<CQ_STAGES - 1>();
       __syncwarp();
-      const uint32_t kraw = wbuf + (ci % STAGES) * STAGE, vraw = kraw + RAWH;
+      const uint32_t kraw = wbuf + (ci % CQ_STAGES) * STAGE, vraw = kraw + RAWH;
       const uint32_t kmeta = kraw + ATT_CHUNK * RB, vmeta = vraw + ATT_CHUNK * RB;
       const int nval = min(ATT_CHUNK, t_end - t_begin - ci * ATT_CHUNK);
       const bool val0 = r < nval, val1 = r + 8 < nval;  // this lane's tokens r and r + 8
-      // (scale, centred zero) of group gi for tokens r and r + 8; zeros past the end
+      // (scale, zero) of group gi for tokens r and r + 8; zeros past the end
       auto load_meta = [&](uint32_t mbase, int gi, float& s0, float& z0, float& s1, float& z1) {
         float a[2], b[2];
 #pragma unroll
         for (int k = 0; k < 2; ++k) {
           const uint32_t ad = mbase + (r + 8 * k) * MB;
-          if (MF32) {
+          if (mf32) {
             const uint2 m = lds64(ad + gi * 8);
             a[k] = __uint_as_float(m.x);
             b[k] = __uint_as_float(m.y);
@@ -949,11 +973,10 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
             b[k] = fm.y;
           }
         }
-        constexpr float OFF = (float)(1 << (BITS - 1));
         s0 = val0 ? a[0] : 0.0f;
-        z0 = val0 ? fmaf(a[0], OFF, b[0]) : 0.0f;
+        z0 = val0 ? b[0] : 0.0f;
         s1 = val1 ? a[1] : 0.0f;
-        z1 = val1 ? fmaf(a[1], OFF, b[1]) : 0.0f;
+        z1 = val1 ? b[1] : 0.0f;
       };
 
       // S^T = K Q^T, folded into sacc at the end of each group
@@ -992,19 +1015,29 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
             const int kk = (sc2 + half) * MPS + u;
 #pragma unroll
             for (int n = 0; n < NH; ++n) mma16816<RMLX_F16>(sgp[n], a[u], qb[n][kk][0], qb[n][kk][1]);
-            if ((((kk + 1) << 4) & (gs - 1)) == 0) {  // the group ends with this k-step
-              const int gi = (kk << 4) >> gs_log2;
+            if (((kk + 1) * 16) % GS == 0) {  // the group ends with this k-step
+              const int gk = kk * 16 / GS;
               float s0, z0, s1, z1;
-              load_meta(kmeta, gi, s0, z0, s1, z1);
+              load_meta(kmeta, gk, s0, z0, s1, z1);
+              // zeros net of the offsets: x sums ride on 1024, y sums on 64
+              const float zx0 = fmaf(s0, -1024.0f, z0), zx1 = fmaf(s1, -1024.0f, z1);
+              const float zy0 = fmaf(s0, -64.0f, z0), zy1 = fmaf(s1, -64.0f, z1);
 #pragma unroll
               for (int n = 0; n < NH; ++n) {
-                const float2 qs = *reinterpret_cast<const float2*>(qgs + gi * 16 + 8 * n + 2 * c);
-                sacc[n][0] = fmaf(s0, sgp[n][0], fmaf(z0, qs.x, sacc[n][0]));
-                sacc[n][1] = fmaf(s0, sgp[n][1], fmaf(z0, qs.y, sacc[n][1]));
-                sacc[n][2] = fmaf(s1, sgp[n][2], fmaf(z1, qs.x, sacc[n][2]));
-                sacc[n][3] = fmaf(s1, sgp[n][3], fmaf(z1, qs.y, sacc[n][3]));
+                const float4 qs = *reinterpret_cast<const float4*>(qgs + gk * 16 + 8 * n + 2 * c);  // x, y of 2 heads
+                float t[4] = {fmaf(s0, sgp[n][0], zx0 * qs.x), fmaf(s0, sgp[n][1], zx0 * qs.z),
+                              fmaf(s1, sgp[n][2], zx1 * qs.x), fmaf(s1, sgp[n][3], zx1 * qs.z)};
+                if (BITS == 4) {
+                  t[0] = fmaf(zy0, qs.y, t[0]);
+                  t[1] = fmaf(zy0, qs.w, t[1]);
+                  t[2] = fmaf(zy1, qs.y, t[2]);
+                  t[3] = fmaf(zy1, qs.w, t[3]);
+                }
 #pragma unroll
-                for (int k = 0; k < 4; ++k) sgp[n][k] = 0.0f;
+                for (int k = 0; k < 4; ++k) {
+                  sacc[n][k] += t[k];
+                  sgp[n][k] = 0.0f;
+                }
               }
             }
           }
@@ -1045,7 +1078,7 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
 
       // O^T += V^T P^T, one group at a time
       uint32_t pb[NH][2];
-      float cz[NH][2], smx = 1.0f;
+      float cz[NH][4], smx = 1.0f;
 #pragma unroll
       for (int sc2 = 0; sc2 < NSEG; sc2 += 2) {
         uint32_t wv[4];  // tokens (2c, 2c+1) | (8+2c, 9+2c) of column sc2, then of column sc2 + 1
@@ -1053,28 +1086,42 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
           const int col = sc2 + half;
-          if (((col * SEGD) & (gs - 1)) == 0) {  // the column starts a group
-            const int gi = (col * SEGD) >> gs_log2;
+          if ((col * SEGD) % GS == 0) {  // the column starts a group
+            const int gv = col * SEGD / GS;
             float s0, z0, s1, z1;
-            load_meta(vmeta, gi, s0, z0, s1, z1);
+            load_meta(vmeta, gv, s0, z0, s1, z1);
             float am = fmaxf(fabsf(s0), fabsf(s1));
             am = fmaxf(am, __shfl_xor_sync(FULL, am, 4));
             am = fmaxf(am, __shfl_xor_sync(FULL, am, 8));
             am = fmaxf(am, __shfl_xor_sync(FULL, am, 16));
             smx = am > 0.0f ? am : 1.0f;
-            const float inv = __frcp_rn(smx), a0 = s0 * inv, a1 = s1 * inv;
+            const float inv = rcp_approx(smx), a0 = s0 * inv, a1 = s1 * inv;
+            const float zc0 = fmaf(s0, OFF, z0) * inv, zc1 = fmaf(s1, OFF, z1) * inv;  // centred zeros / smax
 #pragma unroll
             for (int n = 0; n < NH; ++n) {
-              pb[n][0] = movmatrix_t(pack2<RMLX_F16>(sacc[n][0] * a0, sacc[n][1] * a0));
-              pb[n][1] = movmatrix_t(pack2<RMLX_F16>(sacc[n][2] * a1, sacc[n][3] * a1));
+              const uint32_t x0 = pack2<RMLX_F16>(sacc[n][0] * a0, sacc[n][1] * a0);
+              const uint32_t x1 = pack2<RMLX_F16>(sacc[n][2] * a1, sacc[n][3] * a1);
+              pb[n][0] = movmatrix_t(x0);
+              pb[n][1] = movmatrix_t(x1);
+              const float2 w0 = __half22float2(*reinterpret_cast<const __half2*>(&x0));
+              const float2 w1 = __half22float2(*reinterpret_cast<const __half2*>(&x1));
+              // per head: sum_t P z' / smax, and the sum of the rounded weights
+              float zs[2] = {fmaf(sacc[n][0], zc0, sacc[n][2] * zc1), fmaf(sacc[n][1], zc0, sacc[n][3] * zc1)};
+              float ws[2] = {w0.x + w1.x, w0.y + w1.y};
 #pragma unroll
               for (int e = 0; e < 2; ++e) {
-                float zs = fmaf(sacc[n][e], z0, sacc[n][2 + e] * z1);
-                zs += __shfl_xor_sync(FULL, zs, 4);
-                zs += __shfl_xor_sync(FULL, zs, 8);
-                zs += __shfl_xor_sync(FULL, zs, 16);
-                cz[n][e] = zs * inv;
+#pragma unroll
+                for (int o2 = 4; o2 < 32; o2 <<= 1) {
+                  zs[e] += __shfl_xor_sync(FULL, zs[e], o2);
+                  ws[e] += __shfl_xor_sync(FULL, ws[e], o2);
+                }
               }
+              // rows r and r + 8: codes on 1024 (8-bit, 4-bit low nibbles) or 64 (4-bit high nibbles)
+              const float br = 1024.0f + OFF, br8 = (BITS == 8 ? 1024.0f : 64.0f) + OFF;
+              cz[n][0] = fmaf(-br, ws[0], zs[0]);
+              cz[n][1] = fmaf(-br, ws[1], zs[1]);
+              cz[n][2] = fmaf(-br8, ws[0], zs[0]);
+              cz[n][3] = fmaf(-br8, ws[1], zs[1]);
             }
           }
           const uint32_t lo = wv[2 * half], hi = wv[2 * half + 1];
@@ -1101,7 +1148,7 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
 #pragma unroll
             for (int n = 0; n < NH; ++n) {
               float t[4];
-              mma16816_c(t, a[u], pb[n][0], pb[n][1], cz[n][0], cz[n][1], cz[n][0], cz[n][1]);
+              mma16816_c(t, a[u], pb[n][0], pb[n][1], cz[n][0], cz[n][1], cz[n][2], cz[n][3]);
               float* od = o[n][col * MPS + u];
               od[0] = fmaf(smx, t[0], od[0]);
               od[1] = fmaf(smx, t[1], od[1]);
@@ -1136,8 +1183,10 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
             const int d0 = col * SEGD + 2 * MPS * r;
             uint32_t w[MPS];
 #pragma unroll
-            for (int u = 0; u < MPS; ++u)
-              w[u] = pack2<DT>(o[n][col * MPS + u][e] * il, o[n][col * MPS + u][2 + e] * il);
+            for (int u = 0; u < MPS; ++u) {
+              const float v0 = o[n][col * MPS + u][e] * il, v1 = o[n][col * MPS + u][2 + e] * il;
+              w[u] = bf ? pack2<RMLX_BF16>(v0, v1) : pack2<RMLX_F16>(v0, v1);
+            }
             if constexpr (MPS == 1) *reinterpret_cast<uint32_t*>(ob + d0 * 2) = w[0];
             else *reinterpret_cast<uint2*>(ob + d0 * 2) = make_uint2(w[0], w[1]);
           }
@@ -1245,7 +1294,6 @@ AttnFn attn_kernel_of(const rmlx_pool_config& c) {
 // Quantised pools whose groups span whole k-steps and code columns are read
 // as codes (paged_decode_attn_codes_kernel); the others are dequantised into
 // a tile.
-constexpr int CQ_STAGES = 2;
 constexpr int cq_minb(int nh) { return nh == 1 ? 4 : 2; }  // CTAs per SM the register budget allows
 bool reads_codes(const rmlx_pool_config& c) {
   return (c.quant_bits == 8 && c.group_size >= 16) || (c.quant_bits == 4 && c.group_size >= 32);
@@ -1257,19 +1305,23 @@ size_t attn_codes_smem(int nseq, int stages, int row_bytes, int meta_row_bytes) 
   return scan_bytes + (size_t)ATT_WARPS * (stages * stage + CQ_QS_BYTES);
 }
 
-template <int DT, int HD, int NH>
-AttnFn pick_codes(int bits, bool mf32) {
+template <int HD, int BITS, int NH>
+AttnFn pick_codes_gs(int gs) {
   constexpr int MINB = cq_minb(NH);
-  if (bits == 8) return mf32 ? paged_decode_attn_codes_kernel<DT, HD, 8, true, NH, CQ_STAGES, MINB>
-                             : paged_decode_attn_codes_kernel<DT, HD, 8, false, NH, CQ_STAGES, MINB>;
-  return mf32 ? paged_decode_attn_codes_kernel<DT, HD, 4, true, NH, CQ_STAGES, MINB>
-              : paged_decode_attn_codes_kernel<DT, HD, 4, false, NH, CQ_STAGES, MINB>;
+  if (gs == 16) {
+    if constexpr (BITS == 8) return paged_decode_attn_codes_kernel<HD, 8, 16, NH, MINB>;
+    return nullptr;
+  }
+  if (gs == 32) return paged_decode_attn_codes_kernel<HD, BITS, 32, NH, MINB>;
+  if (gs == 64) return paged_decode_attn_codes_kernel<HD, BITS, 64, NH, MINB>;
+  if constexpr (HD == 128) {
+    if (gs == 128) return paged_decode_attn_codes_kernel<HD, BITS, 128, NH, MINB>;
+  }
+  return nullptr;
 }
 template <int HD, int NH>
 AttnFn pick_codes(const rmlx_pool_config& c) {
-  const bool mf32 = c.meta_dtype == RMLX_F32;
-  return c.dtype == RMLX_BF16 ? pick_codes<RMLX_BF16, HD, NH>(c.quant_bits, mf32)
-                              : pick_codes<RMLX_F16, HD, NH>(c.quant_bits, mf32);
+  return c.quant_bits == 8 ? pick_codes_gs<HD, 8, NH>(c.group_size) : pick_codes_gs<HD, 4, NH>(c.group_size);
 }
 
 // The split kernel a pool's launches use and its dynamic shared memory.
@@ -1283,7 +1335,7 @@ AttnPlan attn_plan(const rmlx_kv_pool* p, int nseq, int G) {
   if (reads_codes(c)) {
     AttnFn fn = hd == 128 ? (G <= 8 ? pick_codes<128, 1>(c) : pick_codes<128, 2>(c))
                           : (G <= 8 ? pick_codes<64, 1>(c) : pick_codes<64, 2>(c));
-    return {fn, attn_codes_smem(nseq, CQ_STAGES, (int)p->row_bytes, (int)p->meta_row_bytes)};
+    if (fn) return {fn, attn_codes_smem(nseq, CQ_STAGES, (int)p->row_bytes, (int)p->meta_row_bytes)};
   }
   return {attn_kernel_of(c), attn_smem(nseq, hd, ATT_STAGES, ATT_QSMEM, c.quant_bits, (int)p->row_bytes,
                                        (int)p->meta_row_bytes)};

@@ -11,6 +11,7 @@ struct PoolGeo {
   int64_t tile_bytes;
   int32_t layers, heads, bs, nblocks;
   int32_t row_bytes, meta_row_bytes;
+  int32_t dtype;  // RMLX_BF16 / RMLX_F16 / RMLX_F32 of the stored (or dequantised) rows
   __device__ __forceinline__ int64_t tile_off(int64_t blk, int l, int kv, int h) const {
     return (((blk * layers + l) * 2 + kv) * heads + h) * tile_bytes;
   }
@@ -110,6 +111,7 @@ struct rmlx_kv_pool {
     g.nblocks = cfg.num_blocks;
     g.row_bytes = (int32_t)row_bytes;
     g.meta_row_bytes = (int32_t)meta_row_bytes;
+    g.dtype = cfg.dtype;
     return g;
   }
 };
