@@ -373,32 +373,6 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
     const int nchunks = (t_end - t_begin + ATT_CHUNK - 1) / ATT_CHUNK;
     const int32_t* btrow = bt + (int64_t)s * bt_stride;
 
-    // Q as A fragments (rows = query heads, zero beyond G): in registers,
-    // or staged in shared memory for ldmatrix at every step.
-    uint32_t qa[QSMEM ? 1 : KT][4];
-    const uint8_t* qbase = q + ((int64_t)s * qheads + (int64_t)h * G) * ROWB;
-    if (QSMEM) {
-#pragma unroll
-      for (int i = 0; i < (ATT_CHUNK * CPR) / 32; ++i) {
-        const int idx = lane + 32 * i, row = idx / CPR, ch = idx % CPR;
-        uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (row < G) v = __ldg(reinterpret_cast<const uint4*>(qbase + (int64_t)row * ROWB + ch * 16));
-        const uint32_t a = qbuf + row * ROWB + ((ch ^ (row & 7)) << 4);
-        asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
-                     : "memory");
-      }
-      __syncwarp();
-    } else {
-#pragma unroll
-      for (int kk = 0; kk < KT; ++kk)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int row = r + (i & 1) * 8, col = kk * 16 + 2 * c + (i >> 1) * 8;
-          qa[kk][i] =
-              row < G ? __ldg(reinterpret_cast<const uint32_t*>(qbase + (int64_t)row * ROWB + col * 2)) : 0u;
-        }
-    }
-
     auto load_chunk = [&](int ci) {
       const uint32_t dst = wbuf + (ci % STAGES) * STAGE;
       const int tc = t_begin + ci * ATT_CHUNK;
@@ -459,6 +433,34 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
       if (ci < nchunks) load_chunk(ci);
       else cp_async_commit();  // keep one group per slot so the wait count stays fixed
     }
+
+    // Q as A fragments (rows = query heads, zero beyond G): in registers,
+    // or staged in shared memory for ldmatrix at every step (while the
+    // first chunks load).
+    uint32_t qa[QSMEM ? 1 : KT][4];
+    const uint8_t* qbase = q + ((int64_t)s * qheads + (int64_t)h * G) * ROWB;
+    if (QSMEM) {
+#pragma unroll
+      for (int i = 0; i < (ATT_CHUNK * CPR) / 32; ++i) {
+        const int idx = lane + 32 * i, row = idx / CPR, ch = idx % CPR;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (row < G) v = __ldg(reinterpret_cast<const uint4*>(qbase + (int64_t)row * ROWB + ch * 16));
+        const uint32_t a = qbuf + row * ROWB + ((ch ^ (row & 7)) << 4);
+        asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                     : "memory");
+      }
+      __syncwarp();
+    } else {
+#pragma unroll
+      for (int kk = 0; kk < KT; ++kk)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int row = r + (i & 1) * 8, col = kk * 16 + 2 * c + (i >> 1) * 8;
+          qa[kk][i] =
+              row < G ? __ldg(reinterpret_cast<const uint32_t*>(qbase + (int64_t)row * ROWB + col * 2)) : 0u;
+        }
+    }
+
     for (int ci = 0; ci < nchunks; ++ci) {
       if (ci + STAGES - 1 < nchunks) load_chunk(ci + STAGES - 1);
       else cp_async_commit();
@@ -733,10 +735,9 @@ __device__ __forceinline__ float rcp_approx(float x) {
 
 // Per warp: per (group, head) the sums of the queries' f16 values over the
 // group's dims riding on 1024 (x) and on 64 (y; 4-bit high nibbles).
-constexpr int CQ_QS_BYTES = 8 * 16 * 8;
-constexpr int CQ_STAGES = 2;  // chunks in flight per warp
+__host__ __device__ constexpr int cq_qs_bytes(int hd, int gs, int nh) { return (hd / gs) * 8 * nh * 8; }
 
-template <int HD, int BITS, int GS, int NH, int MINB>
+template <int HD, int BITS, int GS, int NH, int STAGES, int MINB>
 __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
     paged_decode_attn_codes_kernel(PoolGeo g, int layer, const uint8_t* __restrict__ q, int G,
                                    const int32_t* __restrict__ bt, int bt_stride, const int32_t* __restrict__ lens,
@@ -767,10 +768,10 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
   int32_t* cut = cub + nseq + 1;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const size_t scan_bytes = ((size_t)2 * (nseq + 1) * 4 + 127) & ~(size_t)127;
-  const int WBYTES = CQ_STAGES * STAGE + CQ_QS_BYTES;
+  const int WBYTES = STAGES * STAGE + cq_qs_bytes(HD, GS, NH);
   uint8_t* wgen = smem + scan_bytes + (size_t)warp * WBYTES;
   const uint32_t wbuf = (uint32_t)__cvta_generic_to_shared(wgen);
-  float2* qgs = reinterpret_cast<float2*>(wgen + CQ_STAGES * STAGE);  // [group][head]
+  float2* qgs = reinterpret_cast<float2*>(wgen + STAGES * STAGE);  // [group][8 NH heads]
   pdl_wait();
   pdl_release();
   const int split = pick_split(lens, nseq, g.heads, target, cap_splits, cub, cut);
@@ -790,6 +791,7 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
   const int trow = ((mi & 1) << 3) + (lane & 7);  // the token row this lane addresses in ldmatrix
   const int64_t vdelta = (int64_t)g.heads * g.tile_bytes;
   const bool aligned_blocks = (g.bs % ATT_CHUNK) == 0;
+  // items handed out as in the kernel above
   auto next_item = [&]() -> int64_t {
     unsigned long long v = 0;
     if (lane == 0) v = atomicAdd(work, 1ULL);
@@ -804,9 +806,65 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
     const int nchunks = (t_end - t_begin + ATT_CHUNK - 1) / ATT_CHUNK;
     const int32_t* btrow = bt + (int64_t)s * bt_stride;
 
-    // Queries as B fragments: n-tile n, k-step kk holds head 8n + r at k
-    // positions (2c, 2c+1) and (2c+8, 2c+9); the sums per (group, head)
-    // go to shared memory.
+    // chunks are loaded in order: the block table entry and row of the next one
+    int ld_blk = 0, ld_row = 0;
+    if (aligned_blocks) {
+      ld_blk = t_begin / g.bs;
+      ld_row = t_begin - ld_blk * g.bs;
+    }
+    auto load_chunk = [&](int ci) {
+      const uint32_t dst = wbuf + (ci % STAGES) * STAGE;
+      if (!aligned_blocks) {
+        load_quant_chunk<NSEG>(dst, g, layer, h, btrow, t_begin + ci * ATT_CHUNK, t_end, false, vdelta, lane, err);
+        return;
+      }
+      // the chunk's 16 code rows and 16 meta rows are each a contiguous run of the tile
+      const int32_t blk = __ldg(btrow + ld_blk);
+      const bool ok = blk >= 0 && blk < g.nblocks;
+      if (!ok && lane == 0) atomicOr(err, DEV_ERR_BLOCK);
+      const int nb = ok ? 16 : 0;
+      const uint8_t* tile = ok ? g.base + g.tile_off(blk, layer, 0, h) : g.base;
+      const uint8_t* codes = tile + ld_row * RB;
+#pragma unroll
+      for (int i = 0; i < CU; ++i) {
+        const int u = lane + 32 * i, row = u / NSEG, ch = u % NSEG;
+        const uint32_t so = row * RB + (code_col<NSEG>(row, ch) << 4);
+        const uint8_t* sp = ok ? codes + u * 16 : g.base;
+        cp_async16(dst + so, sp, nb);
+        cp_async16(dst + RAWH + so, ok ? sp + vdelta : g.base, nb);
+      }
+      const uint8_t* meta = tile + (int64_t)g.bs * RB + ld_row * MB;
+      for (int x = lane; x < MB; x += 32) {  // 16 meta rows = MB 16-byte units
+        const uint8_t* sp = ok ? meta + x * 16 : g.base;
+        cp_async16(dst + ATT_CHUNK * RB + x * 16, sp, nb);
+        cp_async16(dst + RAWH + ATT_CHUNK * RB + x * 16, ok ? sp + vdelta : g.base, nb);
+      }
+      cp_async_commit();
+      ld_row += ATT_CHUNK;
+      if (ld_row == g.bs) {
+        ld_row = 0;
+        ++ld_blk;
+      }
+    };
+
+    float o[NH][MT][4];
+#pragma unroll
+    for (int n = 0; n < NH; ++n)
+#pragma unroll
+      for (int d = 0; d < MT; ++d) o[n][d][0] = o[n][d][1] = o[n][d][2] = o[n][d][3] = 0.0f;
+    float mrun[NH][2], lrun[NH][2];  // heads 8n + 2c + e: running max, this lane's share of the sum
+#pragma unroll
+    for (int n = 0; n < NH; ++n) mrun[n][0] = mrun[n][1] = -INFINITY, lrun[n][0] = lrun[n][1] = 0.0f;
+
+#pragma unroll
+    for (int ci = 0; ci < STAGES - 1; ++ci) {
+      if (ci < nchunks) load_chunk(ci);
+      else cp_async_commit();
+    }
+
+    // Queries (while the first chunks load) as B fragments: n-tile n,
+    // k-step kk holds head 8n + r at k positions (2c, 2c+1) and (2c+8,
+    // 2c+9); the sums per (group, head) go to shared memory.
     uint32_t qb[NH][KT][2];
     float fsc[NH][2];  // softmax scale x max|q| of heads 8n + 2c + e
     __syncwarp();  // the previous item's reads of qgs are done
@@ -883,7 +941,7 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
             gy += __shfl_xor_sync(FULL, gy, 1);
             gy += __shfl_xor_sync(FULL, gy, 2);
           }
-          if (c == 0) qgs[(kk * 16 / GS) * 16 + hr] = make_float2(gx, gy);
+          if (c == 0) qgs[(kk * 16 / GS) * 8 * NH + hr] = make_float2(gx, gy);
           gx = gy = 0.0f;
         }
       }
@@ -892,67 +950,12 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
     }
     __syncwarp();
 
-    // chunks are loaded in order: the block table entry and row of the next one
-    int ld_blk = 0, ld_row = 0;
-    if (aligned_blocks) {
-      ld_blk = t_begin / g.bs;
-      ld_row = t_begin - ld_blk * g.bs;
-    }
-    auto load_chunk = [&](int ci) {
-      const uint32_t dst = wbuf + (ci % CQ_STAGES) * STAGE;
-      if (!aligned_blocks) {
-        load_quant_chunk<NSEG>(dst, g, layer, h, btrow, t_begin + ci * ATT_CHUNK, t_end, false, vdelta, lane, err);
-        return;
-      }
-      // the chunk's 16 code rows and 16 meta rows are each a contiguous run of the tile
-      const int32_t blk = __ldg(btrow + ld_blk);
-      const bool ok = blk >= 0 && blk < g.nblocks;
-      if (!ok && lane == 0) atomicOr(err, DEV_ERR_BLOCK);
-      const int nb = ok ? 16 : 0;
-      const uint8_t* tile = ok ? g.base + g.tile_off(blk, layer, 0, h) : g.base;
-      const uint8_t* codes = tile + ld_row * RB;
-#pragma unroll
-      for (int i = 0; i < CU; ++i) {
-        const int u = lane + 32 * i, row = u / NSEG, ch = u % NSEG;
-        const uint32_t so = row * RB + (code_col<NSEG>(row, ch) << 4);
-        const uint8_t* sp = ok ? codes + u * 16 : g.base;
-        cp_async16(dst + so, sp, nb);
-        cp_async16(dst + RAWH + so, ok ? sp + vdelta : g.base, nb);
-      }
-      const uint8_t* meta = tile + (int64_t)g.bs * RB + ld_row * MB;
-      for (int x = lane; x < MB; x += 32) {  // 16 meta rows = MB 16-byte units
-        const uint8_t* sp = ok ? meta + x * 16 : g.base;
-        cp_async16(dst + ATT_CHUNK * RB + x * 16, sp, nb);
-        cp_async16(dst + RAWH + ATT_CHUNK * RB + x * 16, ok ? sp + vdelta : g.base, nb);
-      }
-      cp_async_commit();
-      ld_row += ATT_CHUNK;
-      if (ld_row == g.bs) {
-        ld_row = 0;
-        ++ld_blk;
-      }
-    };
-
-    float o[NH][MT][4];
-#pragma unroll
-    for (int n = 0; n < NH; ++n)
-#pragma unroll
-      for (int d = 0; d < MT; ++d) o[n][d][0] = o[n][d][1] = o[n][d][2] = o[n][d][3] = 0.0f;
-    float mrun[NH][2], lrun[NH][2];  // heads 8n + 2c + e: running max, this lane's share of the sum
-#pragma unroll
-    for (int n = 0; n < NH; ++n) mrun[n][0] = mrun[n][1] = -INFINITY, lrun[n][0] = lrun[n][1] = 0.0f;
-
-#pragma unroll
-    for (int ci = 0; ci < CQ_STAGES - 1; ++ci) {
-      if (ci < nchunks) load_chunk(ci);
-      else cp_async_commit();
-    }
     for (int ci = 0; ci < nchunks; ++ci) {
-      if (ci + CQ_STAGES - 1 < nchunks) load_chunk(ci + CQ_STAGES - 1);
+      if (ci + STAGES - 1 < nchunks) load_chunk(ci + STAGES - 1);
       else cp_async_commit();
-      cp_async_wait<CQ_STAGES - 1>();
+      cp_async_wait<STAGES - 1>();
       __syncwarp();
-      const uint32_t kraw = wbuf + (ci % CQ_STAGES) * STAGE, vraw = kraw + RAWH;
+      const uint32_t kraw = wbuf + (ci % STAGES) * STAGE, vraw = kraw + RAWH;
       const uint32_t kmeta = kraw + ATT_CHUNK * RB, vmeta = vraw + ATT_CHUNK * RB;
       const int nval = min(ATT_CHUNK, t_end - t_begin - ci * ATT_CHUNK);
       const bool val0 = r < nval, val1 = r + 8 < nval;  // this lane's tokens r and r + 8
@@ -1024,7 +1027,7 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
               const float zy0 = fmaf(s0, -64.0f, z0), zy1 = fmaf(s1, -64.0f, z1);
 #pragma unroll
               for (int n = 0; n < NH; ++n) {
-                const float4 qs = *reinterpret_cast<const float4*>(qgs + gk * 16 + 8 * n + 2 * c);  // x, y of 2 heads
+                const float4 qs = *reinterpret_cast<const float4*>(qgs + gk * 8 * NH + 8 * n + 2 * c);  // x, y of 2 heads
                 float t[4] = {fmaf(s0, sgp[n][0], zx0 * qs.x), fmaf(s0, sgp[n][1], zx0 * qs.z),
                               fmaf(s1, sgp[n][2], zx1 * qs.x), fmaf(s1, sgp[n][3], zx1 * qs.z)};
                 if (BITS == 4) {
@@ -1294,28 +1297,30 @@ AttnFn attn_kernel_of(const rmlx_pool_config& c) {
 // Quantised pools whose groups span whole k-steps and code columns are read
 // as codes (paged_decode_attn_codes_kernel); the others are dequantised into
 // a tile.
-constexpr int cq_minb(int nh) { return nh == 1 ? 4 : 2; }  // CTAs per SM the register budget allows
+// CTAs per SM the register budget allows: two head tiles, or many groups,
+// hold more accumulators
+constexpr int cq_minb(int nh, int ng) { return nh == 2 ? 2 : (ng <= 4 ? 4 : 3); }
 bool reads_codes(const rmlx_pool_config& c) {
   return (c.quant_bits == 8 && c.group_size >= 16) || (c.quant_bits == 4 && c.group_size >= 32);
 }
 
-size_t attn_codes_smem(int nseq, int stages, int row_bytes, int meta_row_bytes) {
+constexpr int CQ_STAGES = 2;  // chunks in flight per warp
+size_t attn_codes_smem(int nseq, int stages, int row_bytes, int meta_row_bytes, int qs_bytes) {
   const size_t scan_bytes = ((size_t)2 * (nseq + 1) * 4 + 127) & ~(size_t)127;
   const size_t stage = 2 * ATT_CHUNK * (size_t)(row_bytes + meta_row_bytes);
-  return scan_bytes + (size_t)ATT_WARPS * (stages * stage + CQ_QS_BYTES);
+  return scan_bytes + (size_t)ATT_WARPS * (stages * stage + qs_bytes);
 }
 
 template <int HD, int BITS, int NH>
 AttnFn pick_codes_gs(int gs) {
-  constexpr int MINB = cq_minb(NH);
   if (gs == 16) {
-    if constexpr (BITS == 8) return paged_decode_attn_codes_kernel<HD, 8, 16, NH, MINB>;
+    if constexpr (BITS == 8) return paged_decode_attn_codes_kernel<HD, 8, 16, NH, CQ_STAGES, cq_minb(NH, HD / 16)>;
     return nullptr;
   }
-  if (gs == 32) return paged_decode_attn_codes_kernel<HD, BITS, 32, NH, MINB>;
-  if (gs == 64) return paged_decode_attn_codes_kernel<HD, BITS, 64, NH, MINB>;
+  if (gs == 32) return paged_decode_attn_codes_kernel<HD, BITS, 32, NH, CQ_STAGES, cq_minb(NH, HD / 32)>;
+  if (gs == 64) return paged_decode_attn_codes_kernel<HD, BITS, 64, NH, CQ_STAGES, cq_minb(NH, HD / 64)>;
   if constexpr (HD == 128) {
-    if (gs == 128) return paged_decode_attn_codes_kernel<HD, BITS, 128, NH, MINB>;
+    if (gs == 128) return paged_decode_attn_codes_kernel<HD, BITS, 128, NH, CQ_STAGES, cq_minb(NH, 1)>;
   }
   return nullptr;
 }
@@ -1335,7 +1340,9 @@ AttnPlan attn_plan(const rmlx_kv_pool* p, int nseq, int G) {
   if (reads_codes(c)) {
     AttnFn fn = hd == 128 ? (G <= 8 ? pick_codes<128, 1>(c) : pick_codes<128, 2>(c))
                           : (G <= 8 ? pick_codes<64, 1>(c) : pick_codes<64, 2>(c));
-    if (fn) return {fn, attn_codes_smem(nseq, CQ_STAGES, (int)p->row_bytes, (int)p->meta_row_bytes)};
+    if (fn)
+      return {fn, attn_codes_smem(nseq, CQ_STAGES, (int)p->row_bytes, (int)p->meta_row_bytes,
+                                  cq_qs_bytes(hd, c.group_size, G <= 8 ? 1 : 2))};
   }
   return {attn_kernel_of(c), attn_smem(nseq, hd, ATT_STAGES, ATT_QSMEM, c.quant_bits, (int)p->row_bytes,
                                        (int)p->meta_row_bytes)};
