@@ -733,9 +733,6 @@ __device__ __forceinline__ float rcp_approx(float x) {
   return y;
 }
 
-// Per warp: per (group, head) the sums of the queries' f16 values over the
-// group's dims riding on 1024 (x) and on 64 (y; 4-bit high nibbles).
-__host__ __device__ constexpr int cq_qs_bytes(int hd, int gs, int nh) { return (hd / gs) * 8 * nh * 8; }
 
 template <int HD, int BITS, int GS, int NH, int STAGES, int MINB>
 __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
@@ -768,10 +765,8 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
   int32_t* cut = cub + nseq + 1;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const size_t scan_bytes = ((size_t)2 * (nseq + 1) * 4 + 127) & ~(size_t)127;
-  const int WBYTES = STAGES * STAGE + cq_qs_bytes(HD, GS, NH);
-  uint8_t* wgen = smem + scan_bytes + (size_t)warp * WBYTES;
-  const uint32_t wbuf = (uint32_t)__cvta_generic_to_shared(wgen);
-  float2* qgs = reinterpret_cast<float2*>(wgen + STAGES * STAGE);  // [group][8 NH heads]
+  const int WBYTES = STAGES * STAGE;
+  const uint32_t wbuf = (uint32_t)__cvta_generic_to_shared(smem + scan_bytes) + warp * WBYTES;
   pdl_wait();
   pdl_release();
   const int split = pick_split(lens, nseq, g.heads, target, cap_splits, cub, cut);
@@ -864,91 +859,85 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
 
     // Queries (while the first chunks load) as B fragments: n-tile n,
     // k-step kk holds head 8n + r at k positions (2c, 2c+1) and (2c+8,
-    // 2c+9); the sums per (group, head) go to shared memory.
+    // 2c+9), in f16 after division by the row's max |q|.  Their sums per
+    // group come from MMAs against ones, per lane for heads 8n + 2c, 2c+1
+    // (the S^T columns it holds): qsx over the k positions whose codes ride
+    // on 1024, qsy (4-bit) over those riding on 64.
     uint32_t qb[NH][KT][2];
     float fsc[NH][2];  // softmax scale x max|q| of heads 8n + 2c + e
-    __syncwarp();  // the previous item's reads of qgs are done
+    float qsx[NH][NG][2], qsy[NH][NG][2];
 #pragma unroll
     for (int n = 0; n < NH; ++n) {
       const int hr = 8 * n + r;
       const uint8_t* qrow = q + ((int64_t)s * qheads + (int64_t)h * G + hr) * ROWB;
-      constexpr int NV = HD / 4;  // dimensions per lane: 8-bit 16kk + 4c + (0..3); 4-bit 32j + 8c + (0..7)
-      constexpr int VW = BITS == 8 ? 2 : 4;  // 32-bit words per load
-      float f[NV];
+      constexpr int NW = HD / 8;  // 32-bit words (2 dims) per lane: 8-bit 16kk + 4c + (0..3); 4-bit 32j + 8c + (0..7)
+      uint32_t w[NW];
+      if (BITS == 8) {
 #pragma unroll
-      for (int j = 0; j < NV / (2 * VW); ++j) {
-        uint32_t w[VW];
-        const uint8_t* src = qrow + (BITS == 8 ? (16 * j + 4 * c) : (32 * j + 8 * c)) * 2;
-        if (BITS == 8) {
-          const uint2 v = hr < G ? __ldg(reinterpret_cast<const uint2*>(src)) : make_uint2(0u, 0u);
-          w[0] = v.x;
-          w[1] = v.y;
-        } else {
-          const uint4 v = hr < G ? __ldg(reinterpret_cast<const uint4*>(src)) : make_uint4(0u, 0u, 0u, 0u);
-          w[0] = v.x;
-          w[1] = v.y;
-          w[2 % VW] = v.z;
-          w[3 % VW] = v.w;
+        for (int kk = 0; kk < KT; ++kk) {
+          const uint2 v = hr < G ? __ldg(reinterpret_cast<const uint2*>(qrow + (16 * kk + 4 * c) * 2)) : make_uint2(0u, 0u);
+          w[2 * kk] = v.x;
+          w[2 * kk + 1] = v.y;
         }
+      } else {
 #pragma unroll
-        for (int e = 0; e < VW; ++e) {
-          float2 t2;
-          if (bf) {
-            t2.x = __uint_as_float(w[e] << 16);
-            t2.y = __uint_as_float(w[e] & 0xffff0000u);
-          } else {
-            t2 = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
-          }
-          f[2 * VW * j + 2 * e] = t2.x;
-          f[2 * VW * j + 2 * e + 1] = t2.y;
+        for (int j = 0; j < NSEG; ++j) {
+          const uint4 v = hr < G ? __ldg(reinterpret_cast<const uint4*>(qrow + (32 * j + 8 * c) * 2)) : make_uint4(0u, 0u, 0u, 0u);
+          w[(4 * j) % NW] = v.x;
+          w[(4 * j + 1) % NW] = v.y;
+          w[(4 * j + 2) % NW] = v.z;
+          w[(4 * j + 3) % NW] = v.w;
         }
       }
+      auto unpack = [&](uint32_t x) -> float2 {
+        if (bf) return make_float2(__uint_as_float(x << 16), __uint_as_float(x & 0xffff0000u));
+        return __half22float2(*reinterpret_cast<const __half2*>(&x));
+      };
       float mx = 0.0f;
 #pragma unroll
-      for (int i = 0; i < NV; ++i) mx = fmaxf(mx, fabsf(f[i]));
+      for (int i = 0; i < NW; ++i) {
+        const float2 t2 = unpack(w[i]);
+        mx = fmaxf(mx, fmaxf(fabsf(t2.x), fabsf(t2.y)));
+      }
       mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, 1));
       mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, 2));
       const float msc = mx > 0.0f ? mx : 1.0f, inv = rcp_approx(msc);
 #pragma unroll
-      for (int i = 0; i < NV; ++i) f[i] = __half2float(__float2half_rn(f[i] * inv));
-      // fragments, and the group sums (a group holds whole k-steps)
-      float gx = 0.0f, gy = 0.0f;
+      for (int i = 0; i < NW; ++i) {
+        const float2 t2 = unpack(w[i]);
+        w[i] = pack2<RMLX_F16>(t2.x * inv, t2.y * inv);
+      }
 #pragma unroll
       for (int kk = 0; kk < KT; ++kk) {
-        float p[4];  // the fragment's values: k positions 2c, 2c+1, 2c+8, 2c+9
         if (BITS == 8) {  // k-step kk: dims 16kk + 4c + (0, 1) | (2, 3)
-#pragma unroll
-          for (int i = 0; i < 4; ++i) p[i] = f[4 * kk + i];
+          qb[n][kk][0] = w[2 * kk];
+          qb[n][kk][1] = w[2 * kk + 1];
         } else {  // k-step 2j + u: dims 32j + 8c + (2u, 2u+4) | (2u+1, 2u+5)
           const int j = kk >> 1, u = kk & 1;
-          p[0] = f[8 * j + 2 * u];
-          p[1] = f[8 * j + 2 * u + 4];
-          p[2] = f[8 * j + 2 * u + 1];
-          p[3] = f[8 * j + 2 * u + 5];
+          qb[n][kk][0] = __byte_perm(w[(4 * j + u) % NW], w[(4 * j + 2 + u) % NW], 0x5410);
+          qb[n][kk][1] = __byte_perm(w[(4 * j + u) % NW], w[(4 * j + 2 + u) % NW], 0x7632);
         }
-        qb[n][kk][0] = pack2<RMLX_F16>(p[0], p[1]);
-        qb[n][kk][1] = pack2<RMLX_F16>(p[2], p[3]);
-        if (BITS == 8) {
-          gx += (p[0] + p[1]) + (p[2] + p[3]);
-        } else {  // positions 2c, 2c+1: low nibbles (on 1024); 2c+8, 2c+9: high nibbles (on 64)
-          gx += p[0] + p[1];
-          gy += p[2] + p[3];
+      }
+      constexpr uint32_t ONE2 = 0x3C003C00u;  // (1.0, 1.0) in f16
+      const uint32_t ax[4] = {ONE2, ONE2, BITS == 8 ? ONE2 : 0u, BITS == 8 ? ONE2 : 0u};
+      const uint32_t ay[4] = {0u, 0u, ONE2, ONE2};
+#pragma unroll
+      for (int gg = 0; gg < NG; ++gg) {
+        float dx[4] = {0.f, 0.f, 0.f, 0.f}, dy[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int k = 0; k < GS / 16; ++k) {
+          const int kk = gg * (GS / 16) + k;
+          mma16816<RMLX_F16>(dx, ax, qb[n][kk][0], qb[n][kk][1]);
+          if (BITS == 4) mma16816<RMLX_F16>(dy, ay, qb[n][kk][0], qb[n][kk][1]);
         }
-        if (((kk + 1) * 16) % GS == 0) {  // the group ends with this k-step
-          gx += __shfl_xor_sync(FULL, gx, 1);
-          gx += __shfl_xor_sync(FULL, gx, 2);
-          if (BITS == 4) {
-            gy += __shfl_xor_sync(FULL, gy, 1);
-            gy += __shfl_xor_sync(FULL, gy, 2);
-          }
-          if (c == 0) qgs[(kk * 16 / GS) * 8 * NH + hr] = make_float2(gx, gy);
-          gx = gy = 0.0f;
-        }
+        qsx[n][gg][0] = dx[0];
+        qsx[n][gg][1] = dx[1];
+        qsy[n][gg][0] = dy[0];
+        qsy[n][gg][1] = dy[1];
       }
 #pragma unroll
       for (int e = 0; e < 2; ++e) fsc[n][e] = __shfl_sync(FULL, msc, (2 * c + e) * 4) * scale_log2;
     }
-    __syncwarp();
 
     for (int ci = 0; ci < nchunks; ++ci) {
       if (ci + STAGES - 1 < nchunks) load_chunk(ci + STAGES - 1);
@@ -1027,14 +1016,15 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
               const float zy0 = fmaf(s0, -64.0f, z0), zy1 = fmaf(s1, -64.0f, z1);
 #pragma unroll
               for (int n = 0; n < NH; ++n) {
-                const float4 qs = *reinterpret_cast<const float4*>(qgs + gk * 8 * NH + 8 * n + 2 * c);  // x, y of 2 heads
-                float t[4] = {fmaf(s0, sgp[n][0], zx0 * qs.x), fmaf(s0, sgp[n][1], zx0 * qs.z),
-                              fmaf(s1, sgp[n][2], zx1 * qs.x), fmaf(s1, sgp[n][3], zx1 * qs.z)};
+                const float* qx = qsx[n][gk];
+                const float* qy = qsy[n][gk];
+                float t[4] = {fmaf(s0, sgp[n][0], zx0 * qx[0]), fmaf(s0, sgp[n][1], zx0 * qx[1]),
+                              fmaf(s1, sgp[n][2], zx1 * qx[0]), fmaf(s1, sgp[n][3], zx1 * qx[1])};
                 if (BITS == 4) {
-                  t[0] = fmaf(zy0, qs.y, t[0]);
-                  t[1] = fmaf(zy0, qs.w, t[1]);
-                  t[2] = fmaf(zy1, qs.y, t[2]);
-                  t[3] = fmaf(zy1, qs.w, t[3]);
+                  t[0] = fmaf(zy0, qy[0], t[0]);
+                  t[1] = fmaf(zy0, qy[1], t[1]);
+                  t[2] = fmaf(zy1, qy[0], t[2]);
+                  t[3] = fmaf(zy1, qy[1], t[3]);
                 }
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
@@ -1100,31 +1090,23 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
             smx = am > 0.0f ? am : 1.0f;
             const float inv = rcp_approx(smx), a0 = s0 * inv, a1 = s1 * inv;
             const float zc0 = fmaf(s0, OFF, z0) * inv, zc1 = fmaf(s1, OFF, z1) * inv;  // centred zeros / smax
+            // A of the offsets' MMA: rows r and r + 8 hold -(offset + 2^(bits-1)) for codes
+            // on 1024 (8-bit, 4-bit low nibbles: -1152, -1032) or on 64 (4-bit high nibbles: -72)
+            const uint32_t ar = BITS == 8 ? 0xE480E480u : 0xE408E408u, ar8 = BITS == 8 ? 0xE480E480u : 0xD480D480u;
+            const uint32_t aoff[4] = {ar, ar8, ar, ar8};
 #pragma unroll
             for (int n = 0; n < NH; ++n) {
-              const uint32_t x0 = pack2<RMLX_F16>(sacc[n][0] * a0, sacc[n][1] * a0);
-              const uint32_t x1 = pack2<RMLX_F16>(sacc[n][2] * a1, sacc[n][3] * a1);
-              pb[n][0] = movmatrix_t(x0);
-              pb[n][1] = movmatrix_t(x1);
-              const float2 w0 = __half22float2(*reinterpret_cast<const __half2*>(&x0));
-              const float2 w1 = __half22float2(*reinterpret_cast<const __half2*>(&x1));
-              // per head: sum_t P z' / smax, and the sum of the rounded weights
+              pb[n][0] = movmatrix_t(pack2<RMLX_F16>(sacc[n][0] * a0, sacc[n][1] * a0));
+              pb[n][1] = movmatrix_t(pack2<RMLX_F16>(sacc[n][2] * a1, sacc[n][3] * a1));
+              // per head: sum_t P z' / smax ...
               float zs[2] = {fmaf(sacc[n][0], zc0, sacc[n][2] * zc1), fmaf(sacc[n][1], zc0, sacc[n][3] * zc1)};
-              float ws[2] = {w0.x + w1.x, w0.y + w1.y};
 #pragma unroll
               for (int e = 0; e < 2; ++e) {
 #pragma unroll
-                for (int o2 = 4; o2 < 32; o2 <<= 1) {
-                  zs[e] += __shfl_xor_sync(FULL, zs[e], o2);
-                  ws[e] += __shfl_xor_sync(FULL, ws[e], o2);
-                }
+                for (int o2 = 4; o2 < 32; o2 <<= 1) zs[e] += __shfl_xor_sync(FULL, zs[e], o2);
               }
-              // rows r and r + 8: codes on 1024 (8-bit, 4-bit low nibbles) or 64 (4-bit high nibbles)
-              const float br = 1024.0f + OFF, br8 = (BITS == 8 ? 1024.0f : 64.0f) + OFF;
-              cz[n][0] = fmaf(-br, ws[0], zs[0]);
-              cz[n][1] = fmaf(-br, ws[1], zs[1]);
-              cz[n][2] = fmaf(-br8, ws[0], zs[0]);
-              cz[n][3] = fmaf(-br8, ws[1], zs[1]);
+              // ... less the offsets times the sum of the rounded weights
+              mma16816_c(cz[n], aoff, pb[n][0], pb[n][1], zs[0], zs[1], zs[0], zs[1]);
             }
           }
           const uint32_t lo = wv[2 * half], hi = wv[2 * half + 1];
@@ -1299,16 +1281,16 @@ AttnFn attn_kernel_of(const rmlx_pool_config& c) {
 // a tile.
 // CTAs per SM the register budget allows: two head tiles, or many groups,
 // hold more accumulators
-constexpr int cq_minb(int nh, int ng) { return nh == 2 ? 2 : (ng <= 4 ? 4 : 3); }
+constexpr int cq_minb(int nh, int ng) { return nh == 2 ? 2 : (ng <= 2 ? 4 : 3); }
 bool reads_codes(const rmlx_pool_config& c) {
   return (c.quant_bits == 8 && c.group_size >= 16) || (c.quant_bits == 4 && c.group_size >= 32);
 }
 
 constexpr int CQ_STAGES = 2;  // chunks in flight per warp
-size_t attn_codes_smem(int nseq, int stages, int row_bytes, int meta_row_bytes, int qs_bytes) {
+size_t attn_codes_smem(int nseq, int stages, int row_bytes, int meta_row_bytes) {
   const size_t scan_bytes = ((size_t)2 * (nseq + 1) * 4 + 127) & ~(size_t)127;
   const size_t stage = 2 * ATT_CHUNK * (size_t)(row_bytes + meta_row_bytes);
-  return scan_bytes + (size_t)ATT_WARPS * (stages * stage + qs_bytes);
+  return scan_bytes + (size_t)ATT_WARPS * stages * stage;
 }
 
 template <int HD, int BITS, int NH>
@@ -1341,8 +1323,7 @@ AttnPlan attn_plan(const rmlx_kv_pool* p, int nseq, int G) {
     AttnFn fn = hd == 128 ? (G <= 8 ? pick_codes<128, 1>(c) : pick_codes<128, 2>(c))
                           : (G <= 8 ? pick_codes<64, 1>(c) : pick_codes<64, 2>(c));
     if (fn)
-      return {fn, attn_codes_smem(nseq, CQ_STAGES, (int)p->row_bytes, (int)p->meta_row_bytes,
-                                  cq_qs_bytes(hd, c.group_size, G <= 8 ? 1 : 2))};
+      return {fn, attn_codes_smem(nseq, CQ_STAGES, (int)p->row_bytes, (int)p->meta_row_bytes)};
   }
   return {attn_kernel_of(c), attn_smem(nseq, hd, ATT_STAGES, ATT_QSMEM, c.quant_bits, (int)p->row_bytes,
                                        (int)p->meta_row_bytes)};
