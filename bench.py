@@ -83,7 +83,7 @@ class Workload:
     @property
     def kernel(self):
         if self.attn_g:
-            return "paged_decode_attn_codes_kernel" if self.bits else "paged_decode_attn_kernel"
+            return "paged_decode_attn_codes_kernel" if self.bits else "paged_decode_attn_rows_kernel"
         return "gather_dequant_r1_kernel" if self.bits else "gather_rows_kernel"
 
     @property

@@ -1193,6 +1193,262 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
   }
 }
 
+// ---------------------------------------------------------------------------
+// bf16/f16 pools, with the products transposed as in the codes kernel:
+// tokens are the M rows and the query heads the N columns (one 8-wide
+// n-tile for G <= 8, two up to 16).  Per 16-token chunk and k-step one
+// ldmatrix gives the K rows as an A fragment (no conversion), the queries
+// stay in registers as B fragments for the whole item, P^T reaches the B
+// operand of O^T += V^T P^T through movmatrix, and ldmatrix.trans gives V^T.
+// Against the kernel above: half the MMAs, half the O registers, no query
+// tile in shared memory, so three CTAs of four warps fit an SM (16 KiB of
+// stages per warp).
+template <int DT, int HD, int NH, int STAGES, int MINB>
+__global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
+    paged_decode_attn_rows_kernel(PoolGeo g, int layer, const uint8_t* __restrict__ q, int G,
+                                  const int32_t* __restrict__ bt, int bt_stride, const int32_t* __restrict__ lens,
+                                  int nseq, int64_t target, float scale_log2, float* __restrict__ part_o,
+                                  float* __restrict__ part_ml, int64_t cap_splits, uint8_t* __restrict__ out,
+                                  int gs_log2, unsigned long long* __restrict__ work, int32_t* err) {
+  constexpr int ROWB = HD * 2;  // bytes of a K, V, query or output row
+  constexpr int CPR = ROWB / 16;
+  constexpr int KT = HD / 16;   // k-steps of S^T, and m-tiles of O^T
+  constexpr int STAGE = 2 * ATT_CHUNK * ROWB;  // K rows then V rows, 16-byte columns XOR-swizzled
+  constexpr unsigned FULL = 0xffffffffu;
+  static_assert(CPR >= 8 && (NH == 1 || NH == 2), "shape");
+  extern __shared__ __align__(128) uint8_t smem[];
+  int32_t* cub = reinterpret_cast<int32_t*>(smem);
+  int32_t* cut = cub + nseq + 1;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const size_t scan_bytes = ((size_t)2 * (nseq + 1) * 4 + 127) & ~(size_t)127;
+  const uint32_t wbuf = (uint32_t)__cvta_generic_to_shared(smem + scan_bytes) + warp * STAGES * STAGE;
+  pdl_wait();
+  pdl_release();
+  const int split = pick_split(lens, nseq, g.heads, target, cap_splits, cub, cut);
+  const int64_t nsplit = cub[nseq];
+  if (nsplit > cap_splits) {
+    if (threadIdx.x == 0) atomicOr(err, DEV_ERR_WORKSPACE);
+    return;
+  }
+  const int64_t items = nsplit * g.heads;
+  const int qheads = g.heads * G;
+  for (int64_t s0 = (int64_t)blockIdx.x * ATT_WARPS + warp; s0 < nseq; s0 += (int64_t)gridDim.x * ATT_WARPS)
+    if (cut[s0 + 1] == cut[s0]) {
+      uint4* o4 = reinterpret_cast<uint4*>(out + s0 * qheads * ROWB);
+      for (int x = lane; x < qheads * CPR; x += 32) o4[x] = make_uint4(0u, 0u, 0u, 0u);
+    }
+  const int r = lane >> 2, c = lane & 3, mi = lane >> 3;
+  // ldmatrix row addresses: K (A of S^T) takes matrices (tokens 0-7 | 8-15) x
+  // (k 0-7 | 8-15); V^T (A of O^T) takes (dims 0-7 | 8-15) x (tokens 0-7 | 8-15)
+  const int krow = ((mi & 1) << 3) + (lane & 7), kcol = mi >> 1;
+  const int vrow = ((mi >> 1) << 3) + (lane & 7), vcol = mi & 1;
+  const int64_t vdelta = (int64_t)g.heads * g.tile_bytes;
+  const bool aligned_blocks = (g.bs % ATT_CHUNK) == 0;
+  auto next_item = [&]() -> int64_t {
+    unsigned long long v = 0;
+    if (lane == 0) v = atomicAdd(work, 1ULL);
+    return (int64_t)__shfl_sync(FULL, v, 0);
+  };
+  for (int64_t it = next_item(); it < items; it = next_item()) {
+    const int h = (int)(it % g.heads);
+    const int64_t sg = it / g.heads;
+    const int s = find_seq(cub, nseq, sg);
+    const int t_begin = (int)(sg - cub[s]) * split;
+    const int t_end = min(cut[s + 1] - cut[s], t_begin + split);
+    const int nchunks = (t_end - t_begin + ATT_CHUNK - 1) / ATT_CHUNK;
+    const int32_t* btrow = bt + (int64_t)s * bt_stride;
+
+    int ld_blk = 0, ld_row = 0;  // chunks load in order: the block table entry and row of the next one
+    if (aligned_blocks) {
+      ld_blk = t_begin / g.bs;
+      ld_row = t_begin - ld_blk * g.bs;
+    }
+    auto load_chunk = [&](int ci) {
+      const uint32_t dst = wbuf + (ci % STAGES) * STAGE;
+      if (aligned_blocks) {
+        // the chunk's 16 rows are contiguous in one K tile (and one V tile)
+        const int tc = t_begin + ci * ATT_CHUNK;
+        const int32_t blk = __ldg(btrow + ld_blk);
+        const bool ok = blk >= 0 && blk < g.nblocks;
+        if (!ok && lane == 0) atomicOr(err, DEV_ERR_BLOCK);
+        const uint8_t* src = ok ? g.base + g.tile_off(blk, layer, 0, h) + (int64_t)ld_row * ROWB : g.base;
+#pragma unroll
+        for (int i = 0; i < (ATT_CHUNK * CPR) / 32; ++i) {
+          const int idx = lane + 32 * i, row = idx / CPR, ch = idx % CPR;
+          const int n = (ok && tc + row < t_end) ? 16 : 0;
+          const uint32_t so = row * ROWB + ((ch ^ (row & 7)) << 4);
+          const uint8_t* p = n ? src + row * ROWB + ch * 16 : g.base;
+          cp_async16(dst + so, p, n);
+          cp_async16(dst + ATT_CHUNK * ROWB + so, n ? p + vdelta : g.base, n);
+        }
+        ld_row += ATT_CHUNK;
+        if (ld_row == g.bs) {
+          ld_row = 0;
+          ++ld_blk;
+        }
+      } else {
+        // lanes 0..15 locate row (lane & 15); the others take it by shuffle
+        const int t = t_begin + ci * ATT_CHUNK + (lane & 15);
+        const uint8_t* src = g.base;
+        int nb = 0;
+        if (t < t_end) {
+          const int32_t blk = __ldg(btrow + t / g.bs);
+          if (blk >= 0 && blk < g.nblocks) {
+            src = g.base + g.tile_off(blk, layer, 0, h) + (int64_t)(t % g.bs) * ROWB;
+            nb = 16;
+          } else if (lane < 16) {
+            atomicOr(err, DEV_ERR_BLOCK);
+          }
+        }
+        const unsigned long long sp = reinterpret_cast<unsigned long long>(src);
+#pragma unroll
+        for (int i = 0; i < (ATT_CHUNK * CPR) / 32; ++i) {
+          const int idx = lane + 32 * i, row = idx / CPR, ch = idx % CPR;
+          const uint8_t* rp = reinterpret_cast<const uint8_t*>(__shfl_sync(FULL, sp, row));
+          const int n = __shfl_sync(FULL, nb, row);
+          const uint32_t so = row * ROWB + ((ch ^ (row & 7)) << 4);
+          cp_async16(dst + so, n ? rp + ch * 16 : g.base, n);
+          cp_async16(dst + ATT_CHUNK * ROWB + so, n ? rp + vdelta + ch * 16 : g.base, n);
+        }
+      }
+      cp_async_commit();
+    };
+
+    float o[NH][KT][4];  // O^T: m-tile mt, rows r and r + 8 = dims 16 mt + r, + 8; columns heads 8n + 2c, + 1
+#pragma unroll
+    for (int n = 0; n < NH; ++n)
+#pragma unroll
+      for (int d = 0; d < KT; ++d) o[n][d][0] = o[n][d][1] = o[n][d][2] = o[n][d][3] = 0.0f;
+    float mrun[NH][2], lrun[NH][2];  // heads 8n + 2c + e: running max, this lane's share of the sum
+#pragma unroll
+    for (int n = 0; n < NH; ++n) mrun[n][0] = mrun[n][1] = -INFINITY, lrun[n][0] = lrun[n][1] = 0.0f;
+
+#pragma unroll
+    for (int ci = 0; ci < STAGES - 1; ++ci) {
+      if (ci < nchunks) load_chunk(ci);
+      else cp_async_commit();
+    }
+
+    // queries as B fragments (while the first chunks load): n-tile n, k-step
+    // kk holds head 8n + r at dims 16kk + 2c, +1 and 16kk + 8 + 2c, +1
+    uint32_t qb[NH][KT][2];
+#pragma unroll
+    for (int n = 0; n < NH; ++n) {
+      const int hr = 8 * n + r;
+      const uint8_t* qrow = q + ((int64_t)s * qheads + (int64_t)h * G + hr) * ROWB;
+#pragma unroll
+      for (int kk = 0; kk < KT; ++kk) {
+        qb[n][kk][0] = hr < G ? __ldg(reinterpret_cast<const uint32_t*>(qrow + (16 * kk + 2 * c) * 2)) : 0u;
+        qb[n][kk][1] = hr < G ? __ldg(reinterpret_cast<const uint32_t*>(qrow + (16 * kk + 8 + 2 * c) * 2)) : 0u;
+      }
+    }
+
+    for (int ci = 0; ci < nchunks; ++ci) {
+      if (ci + STAGES - 1 < nchunks) load_chunk(ci + STAGES - 1);
+      else cp_async_commit();
+      cp_async_wait<STAGES - 1>();
+      __syncwarp();
+      const uint32_t kb = wbuf + (ci % STAGES) * STAGE, vb = kb + ATT_CHUNK * ROWB;
+      const int nval = min(ATT_CHUNK, t_end - t_begin - ci * ATT_CHUNK);
+      const bool val0 = r < nval, val1 = r + 8 < nval;  // this lane's tokens r and r + 8
+
+      // S^T = K Q^T
+      float sacc[NH][4];
+#pragma unroll
+      for (int n = 0; n < NH; ++n) sacc[n][0] = sacc[n][1] = sacc[n][2] = sacc[n][3] = 0.0f;
+#pragma unroll
+      for (int kk = 0; kk < KT; ++kk) {
+        uint32_t a[4];
+        const int ch = 2 * kk + kcol;
+        ldsm_x4(kb + krow * ROWB + ((ch ^ (krow & 7)) << 4), a[0], a[1], a[2], a[3]);
+#pragma unroll
+        for (int n = 0; n < NH; ++n) mma16816<DT>(sacc[n], a, qb[n][kk][0], qb[n][kk][1]);
+      }
+      // online softmax (log2 domain) per head over the chunk's tokens
+      bool rescale = false;
+      float al[NH][2];
+#pragma unroll
+      for (int n = 0; n < NH; ++n)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float x0 = val0 ? sacc[n][e] * scale_log2 : -INFINITY;
+          const float x1 = val1 ? sacc[n][2 + e] * scale_log2 : -INFINITY;
+          float mx = fmaxf(x0, x1);
+          mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, 4));
+          mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, 8));
+          mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, 16));
+          const float nm = fmaxf(mrun[n][e], mx);  // finite: every chunk has a valid token
+          al[n][e] = ex2(mrun[n][e] - nm);
+          mrun[n][e] = nm;
+          sacc[n][e] = ex2(x0 - nm);
+          sacc[n][2 + e] = ex2(x1 - nm);
+          lrun[n][e] = lrun[n][e] * al[n][e] + (sacc[n][e] + sacc[n][2 + e]);
+          rescale |= al[n][e] != 1.0f;
+        }
+      if (__any_sync(FULL, rescale)) {
+#pragma unroll
+        for (int n = 0; n < NH; ++n)
+#pragma unroll
+          for (int d = 0; d < KT; ++d) {
+            o[n][d][0] *= al[n][0];
+            o[n][d][1] *= al[n][1];
+            o[n][d][2] *= al[n][0];
+            o[n][d][3] *= al[n][1];
+          }
+      }
+      // O^T += V^T P^T: P (rounded to the pool's type) transposed in registers
+      uint32_t pb[NH][2];
+#pragma unroll
+      for (int n = 0; n < NH; ++n) {
+        pb[n][0] = movmatrix_t(pack2<DT>(sacc[n][0], sacc[n][1]));
+        pb[n][1] = movmatrix_t(pack2<DT>(sacc[n][2], sacc[n][3]));
+      }
+#pragma unroll
+      for (int mt = 0; mt < KT; ++mt) {
+        uint32_t a[4];
+        const int ch = 2 * mt + vcol;
+        ldsm_x4_t(vb + vrow * ROWB + ((ch ^ (vrow & 7)) << 4), a[0], a[1], a[2], a[3]);
+#pragma unroll
+        for (int n = 0; n < NH; ++n) mma16816<DT>(o[n][mt], a, pb[n][0], pb[n][1]);
+      }
+      __syncwarp();  // the stage is overwritten by the next load
+    }
+    cp_async_wait<0>();
+    __syncwarp();
+
+    const int nsp = cub[s + 1] - cub[s];
+#pragma unroll
+    for (int n = 0; n < NH; ++n)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        float lt = lrun[n][e];
+        lt += __shfl_xor_sync(FULL, lt, 4);
+        lt += __shfl_xor_sync(FULL, lt, 8);
+        lt += __shfl_xor_sync(FULL, lt, 16);
+        const int hq = 8 * n + 2 * c + e;  // query head within the group
+        if (hq >= G) continue;
+        if (nsp == 1) {
+          const float il = 1.0f / lt;
+          uint8_t* ob = out + ((int64_t)s * qheads + (int64_t)h * G + hq) * ROWB;
+#pragma unroll
+          for (int mt = 0; mt < KT; ++mt) {
+            const uint32_t w = pack2<DT>(o[n][mt][e] * il, o[n][mt][2 + e] * il);
+            *reinterpret_cast<uint16_t*>(ob + (16 * mt + r) * 2) = (uint16_t)(w & 0xffffu);
+            *reinterpret_cast<uint16_t*>(ob + (16 * mt + 8 + r) * 2) = (uint16_t)(w >> 16);
+          }
+        } else {
+          float* po = part_o + (it * (int64_t)G + hq) * HD;
+#pragma unroll
+          for (int mt = 0; mt < KT; ++mt) {
+            po[16 * mt + r] = o[n][mt][e];
+            po[16 * mt + 8 + r] = o[n][mt][2 + e];
+          }
+          if (r == 0) *reinterpret_cast<float2*>(part_ml + it * (int64_t)2 * G + 2 * hq) = make_float2(mrun[n][e], lt);
+        }
+      }
+  }
+}
+
 // One warp per (sequence, query head) of the sequences held by two or more
 // splits (the split kernel wrote the others): combine_splits.
 template <int DT, int HD>
@@ -1237,10 +1493,12 @@ using AttnFn = void (*)(PoolGeo, int, const uint8_t*, int, const int32_t*, int, 
 using CombineFn = void (*)(const int32_t*, int, int64_t, int, int, const float*, const float*, uint8_t*, int64_t,
                            unsigned long long*);
 
-// Work items a launch wants (about three per resident warp) before it
-// halves its split size.
-int64_t attn_target(AttnFn fa, size_t smem, int num_sms) {
-  return 3 * (int64_t)persistent_grid(fa, ATT_WARPS * 32, smem, num_sms) * ATT_WARPS;
+// Work items a launch wants before it halves its split size: items_x2 / 2
+// per resident warp.  Fewer, longer items save per-item work (queries,
+// partials, combine); more items even out the tail.  Measured per kernel:
+// 1.5 for the bf16/f16 and 8-bit kernels, 3 for the 4-bit one.
+int64_t attn_target(AttnFn fa, size_t smem, int num_sms, int items_x2) {
+  return (int64_t)items_x2 * persistent_grid(fa, ATT_WARPS * 32, smem, num_sms) * ATT_WARPS / 2;
 }
 
 // The configuration the dispatch uses: stages in flight per warp, CTAs per
@@ -1311,10 +1569,24 @@ AttnFn pick_codes(const rmlx_pool_config& c) {
   return c.quant_bits == 8 ? pick_codes_gs<HD, 8, NH>(c.group_size) : pick_codes_gs<HD, 4, NH>(c.group_size);
 }
 
+// bf16/f16 pools: the transposed kernel, three CTAs of four warps per SM
+// (two with two head tiles: more accumulators).
+constexpr int RW_STAGES = 2;
+template <int DT, int HD>
+AttnFn pick_rows(int G) {
+  return G <= 8 ? paged_decode_attn_rows_kernel<DT, HD, 1, RW_STAGES, 3>
+                : paged_decode_attn_rows_kernel<DT, HD, 2, RW_STAGES, 2>;
+}
+size_t attn_rows_smem(int nseq, int hd) {
+  const size_t scan_bytes = ((size_t)2 * (nseq + 1) * 4 + 127) & ~(size_t)127;
+  return scan_bytes + (size_t)ATT_WARPS * RW_STAGES * 2 * ATT_CHUNK * hd * 2;
+}
+
 // The split kernel a pool's launches use and its dynamic shared memory.
 struct AttnPlan {
   AttnFn fn;
   size_t smem;
+  int items_x2;  // work items per resident warp, times 2 (attn_target)
 };
 AttnPlan attn_plan(const rmlx_kv_pool* p, int nseq, int G) {
   const rmlx_pool_config& c = p->cfg;
@@ -1323,10 +1595,17 @@ AttnPlan attn_plan(const rmlx_kv_pool* p, int nseq, int G) {
     AttnFn fn = hd == 128 ? (G <= 8 ? pick_codes<128, 1>(c) : pick_codes<128, 2>(c))
                           : (G <= 8 ? pick_codes<64, 1>(c) : pick_codes<64, 2>(c));
     if (fn)
-      return {fn, attn_codes_smem(nseq, CQ_STAGES, (int)p->row_bytes, (int)p->meta_row_bytes)};
+      return {fn, attn_codes_smem(nseq, CQ_STAGES, (int)p->row_bytes, (int)p->meta_row_bytes),
+              c.quant_bits == 8 ? 3 : 6};
   }
-  return {attn_kernel_of(c), attn_smem(nseq, hd, ATT_STAGES, ATT_QSMEM, c.quant_bits, (int)p->row_bytes,
-                                       (int)p->meta_row_bytes)};
+  if (!c.quant_bits) {
+    const bool bf = c.dtype == RMLX_BF16;
+    AttnFn fn = hd == 128 ? (bf ? pick_rows<RMLX_BF16, 128>(G) : pick_rows<RMLX_F16, 128>(G))
+                          : (bf ? pick_rows<RMLX_BF16, 64>(G) : pick_rows<RMLX_F16, 64>(G));
+    return {fn, attn_rows_smem(nseq, hd), 3};
+  }
+  return {attn_kernel_of(c),
+          attn_smem(nseq, hd, ATT_STAGES, ATT_QSMEM, c.quant_bits, (int)p->row_bytes, (int)p->meta_row_bytes), 6};
 }
 }  // namespace
 
@@ -1345,7 +1624,7 @@ rmlx_status rmlx_kv_attention_workspace_size(const rmlx_kv_pool* p, int32_t q_he
     const AttnPlan plan = attn_plan(p, num_seqs, q_heads_per_kv);
     DeviceGuard dg(p->device);
     if (plan.smem <= 227 * 1024 && prepare_smem(plan.fn, plan.smem) == RMLX_OK) {
-      const int64_t target = attn_target(plan.fn, plan.smem, p->num_sms);
+      const int64_t target = attn_target(plan.fn, plan.smem, p->num_sms, plan.items_x2);
       splits = std::max<int64_t>(splits, 4 * ((target + c.num_kv_heads - 1) / c.num_kv_heads) + num_seqs);
     }
   }
@@ -1399,7 +1678,7 @@ rmlx_status rmlx_kv_decode_attention(rmlx_kv_pool* p, int32_t layer, const void*
   rmlx_status s;
   if ((s = prepare_smem(fa, smem)) != RMLX_OK) return s;
   const int grid = persistent_grid(fa, ATT_WARPS * 32, smem, p->num_sms);
-  const int64_t target = attn_target(fa, smem, p->num_sms);
+  const int64_t target = attn_target(fa, smem, p->num_sms, plan.items_x2);
   const float scale_log2 = softmax_scale * 1.4426950408889634f;  // log2(e)
   cudaError_t e = launch_pdl(fa, dim3(grid), dim3(ATT_WARPS * 32), smem, st, p->geo(), (int)layer,
                              static_cast<const uint8_t*>(q), G, block_tables, (int)block_table_stride, seq_lens,
