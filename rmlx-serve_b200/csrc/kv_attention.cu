@@ -1517,15 +1517,15 @@ size_t attn_smem(int nseq, int hd, int stages, bool qsmem, int bits, int row_byt
                                            (qsmem ? ATT_CHUNK * rowb : 0));
 }
 
+// Quantised pools whose groups are too small to read as codes: the kernel
+// that dequantises into a tile.
 template <int DT, int HD>
 AttnFn pick_attn(int bits, bool mf32) {
   if (bits == 8) return mf32 ? paged_decode_attn_kernel<DT, HD, ATT_STAGES, ATT_MINB, ATT_QSMEM, 8, true>
                              : paged_decode_attn_kernel<DT, HD, ATT_STAGES, ATT_MINB, ATT_QSMEM, 8, false>;
-  if (bits == 4) return mf32 ? paged_decode_attn_kernel<DT, HD, ATT_STAGES, ATT_MINB, ATT_QSMEM, 4, true>
-                             : paged_decode_attn_kernel<DT, HD, ATT_STAGES, ATT_MINB, ATT_QSMEM, 4, false>;
-  return paged_decode_attn_kernel<DT, HD, ATT_STAGES, ATT_MINB, ATT_QSMEM>;
+  return mf32 ? paged_decode_attn_kernel<DT, HD, ATT_STAGES, ATT_MINB, ATT_QSMEM, 4, true>
+              : paged_decode_attn_kernel<DT, HD, ATT_STAGES, ATT_MINB, ATT_QSMEM, 4, false>;
 }
-
 
 AttnFn attn_kernel_of(const rmlx_pool_config& c) {
   const bool bf = c.dtype == RMLX_BF16, mf32 = c.meta_dtype == RMLX_F32;
