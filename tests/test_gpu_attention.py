@@ -23,7 +23,7 @@ import pytest
 
 import oracle as orc
 import rmlx_kv
-from helpers import block_tables, to_dev
+from helpers import ESIZE, block_tables, to_dev
 
 pytestmark = pytest.mark.gpu
 
@@ -49,6 +49,27 @@ def _reference(pool, layer, q, G, bt, lens, scale, dt, cuda):
     torch.cuda.synchronize()
     k = orc.dtype_to_f32(ok.cpu().numpy().view(np.uint16)[:tot * H * D], dt).astype(np.float64)
     v = orc.dtype_to_f32(ov.cpu().numpy().view(np.uint16)[:tot * H * D], dt).astype(np.float64)
+    return _attend(k, v, q, G, lens, scale, dt, H, D)
+
+
+def _reference_exact(pool, layer, q, G, bt, lens, scale, dt, bits, gs, meta):
+    """float64 attention over the oracle's f32 dequantisation of the pool's
+    bytes (the dequantised rows are not rounded to the pool's type)."""
+    c = pool.cfg
+    H, D = c.num_kv_heads, c.head_dim
+    g = orc.Geo(c.num_layers, H, D, c.block_size, c.num_blocks, ESIZE[dt], bits=bits, group_size=gs,
+                meta_bytes=4 if meta == orc.F32 else 2)
+    host = pool.read()
+    tot = int(lens.sum())
+    ek, ev = np.zeros(max(tot * H * D, 1), np.float32), np.zeros(max(tot * H * D, 1), np.float32)
+    assert orc.paged_gather_dequant(host, g, layer, bt, bt.shape[1], lens.astype(np.int32), ek, ev, orc.F32) == 0
+    return _attend(ek[:tot * H * D].astype(np.float64), ev[:tot * H * D].astype(np.float64), q, G, lens, scale, dt,
+                   H, D)
+
+
+def _attend(k, v, q, G, lens, scale, dt, H, D):
+    """softmax(scale q K^T) V per sequence and query head in float64, from
+    K/V gathered as [sequence][head][token][dim]."""
     qf = orc.dtype_to_f32(q, dt).astype(np.float64).reshape(len(lens), H * G, D)
     out = np.zeros_like(qf)
     o = 0
@@ -157,9 +178,15 @@ def test_bad_block_id_flagged(cuda):
     pool.close()
 
 
-def run_attn_quant(cuda, L, H, D, bs, N, dt, G, lens, seed, bits, gs, meta, layer=0):
+def run_attn_quant(cuda, L, H, D, bs, N, dt, G, lens, seed, bits, gs, meta, layer=0, kscale=1.0, vscale=1.0,
+                   shift=0.0, exact_ref=False):
     """Quantised pool filled through the quantise-on-append path; the
-    reference reads the rows the dequantising gather returns."""
+    reference reads the rows the dequantising gather returns (rounded to the
+    pool's type), or with exact_ref the oracle's f32 dequantisation of the
+    same pool bytes.  K = kscale N(0,1) + shift, V = vscale N(0,1) + shift,
+    and the queries are divided by kscale so that the logits stay of order
+    one.  The tolerances grow with the largest |V|, and the RMS bound also
+    allows for the output's own rounding to the pool's type."""
     import torch
     from helpers import rand_rows, slots_for
     rng = np.random.default_rng(seed)
@@ -170,25 +197,33 @@ def run_attn_quant(cuda, L, H, D, bs, N, dt, G, lens, seed, bits, gs, meta, laye
     pos = [(s, p) for s in range(len(lens)) for p in range(int(lens[s]))]
     if pos:
         T = len(pos)
-        k = rand_rows(rng, (L, T, H, D), dt)  # N(0,1): the tolerance above assumes |V| <~ 4.5
-        v = rand_rows(rng, (L, T, H, D), dt)
+        def vals(sc):
+            x = rng.standard_normal((L, T, H, D), dtype=np.float32) * np.float32(sc) + np.float32(shift)
+            return orc.f32_to_dtype(x, dt)
+        k = vals(kscale)  # N(0,1) at scale 1, shift 0: the tolerance above assumes |V| <~ 4.5
+        v = vals(vscale)
         pool.append(to_dev(k), to_dev(v), to_dev(slots_for(bt, bs, pos)), T)
-    q = orc.f32_to_dtype(rng.standard_normal((len(lens), H * G, D), dtype=np.float32), dt)
-    scale = 1.0 / np.sqrt(D)
+    q = orc.f32_to_dtype(rng.standard_normal((len(lens), H * G, D), dtype=np.float32) / np.float32(kscale), dt)
+    sm_scale = 1.0 / np.sqrt(D)
     ws = torch.empty(max(pool.attention_workspace_size(G, len(lens), int(lens.sum())), 16), dtype=torch.uint8,
                      device=cuda)
     out = torch.full((len(lens), H * G, D), -7, dtype=torch.int16, device=cuda)
     pool.decode_attention(layer, to_dev(q), G, to_dev(bt), bt.shape[1], to_dev(lens.astype(np.int32)), len(lens),
-                          scale, out, ws)
+                          sm_scale, out, ws)
     torch.cuda.synchronize()
     assert pool.check() == 0
     got = orc.dtype_to_f32(out.cpu().numpy().view(np.uint16), dt).astype(np.float64)
-    want = _reference(pool, layer, q, G, bt, lens, scale, dt, cuda)
+    if exact_ref:
+        want = _reference_exact(pool, layer, q, G, bt, lens, sm_scale, dt, bits, gs, meta)
+    else:
+        want = _reference(pool, layer, q, G, bt, lens, sm_scale, dt, cuda)
     err = np.abs(got - want)
     mx, rms = TOL[dt]
+    grow = (4.5 * abs(vscale) + abs(shift)) / 4.5
+    out_ulp = (2.0 ** -8 if dt == orc.BF16 else 2.0 ** -11) * np.abs(want).max()  # of the largest output
     assert np.isfinite(got).all()
-    assert err.max() <= mx, f"max abs error {err.max()}"
-    assert np.sqrt((err ** 2).mean()) <= rms
+    assert err.max() <= mx * grow, f"max abs error {err.max()}"
+    assert np.sqrt((err ** 2).mean()) <= rms * grow + out_ulp / 2, f"rms error {np.sqrt((err ** 2).mean())}"
     assert (got[lens == 0] == 0).all()
     pool.close()
 
@@ -210,6 +245,19 @@ def test_quantised_block_sizes_and_groups(cuda, bs, D, gs, dt):
     N = 700 // bs + 40
     for bits in (8, 4):
         run_attn_quant(cuda, 1, 2, D, bs, N, dt, 8, [3, 16, 31, 300], 80 + bs + bits, bits, gs, orc.F16)
+
+
+@pytest.mark.parametrize("kscale,vscale,shift,meta", [(1e-3, 1e-3, 0.0, orc.F32), (1e-3, 1e-3, 0.0, orc.F16),
+                                                       (300.0, 300.0, 0.0, orc.F32), (1.0, 1.0, 40.0, orc.F16)])
+def test_quantised_value_ranges(cuda, kscale, vscale, shift, meta):
+    """K/V far from unit scale (with f16 scale/zero, 1e-3 values give
+    scales below f16's normal range) and a large common offset: the
+    scale/zero folds and the per-chunk normalisation of the weights keep
+    the error relative to |V|.  The reference is the oracle's exact
+    dequantisation."""
+    for bits in (8, 4):
+        run_attn_quant(cuda, 1, 2, 128, 16, 120, orc.BF16, 4, [7, 100, 500], 95 + bits, bits, 64, meta,
+                       kscale=kscale, vscale=vscale, shift=shift, exact_ref=True)
 
 
 @pytest.mark.parametrize("G", [1, 12, 16])
