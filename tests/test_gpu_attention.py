@@ -17,6 +17,11 @@ P s / smax are rounded to f16 (2^-12) instead of P to the pool's type; the
 dequantised rows themselves are never rounded, while the reference reads
 them rounded to the pool's type (2^-9 for bf16, 2^-12 for f16).  The same
 bounds hold.
+
+Value-range cases (K/V scaled by 1e-3 or 300, or offset by 40) compare with
+float64 attention over the oracle's exact f32 dequantisation instead; their
+bounds scale with the largest |V|, and the RMS bound adds half an ulp of the
+largest output, which the output's own rounding to the pool's type costs.
 """
 import numpy as np
 import pytest
