@@ -69,6 +69,7 @@ class Workload:
     dtype: int = BF16
     lens: tuple = ()  # fixed prompt lengths (instead of uniform in [ctx_lo, ctx_hi])
     min_blocks: int = 0  # pool at least this large
+    graph: bool = False  # latency-bound: the timed steps are captured once in a CUDA graph and replayed
 
     # bytes of one token's rows of the local heads
     def in_row(self, h):
@@ -112,7 +113,7 @@ WORKLOADS = {
         "config1", "KV append+gather HBM GB/s (1 layer, 4 sequences; latency-bound: see us_per_step)",
         "the reference's own case: 1 layer x 8 KV heads x 128, block 16, fp16, pool 256 blocks, 4 sequences with "
         "prompts 37/128/255/512, 1 token appended per sequence per step, then the gather of the layer",
-        seed=0x5EED + 1, layers=1, batch=4, lens=(37, 128, 255, 512), dtype=F16, min_blocks=256),
+        seed=0x5EED + 1, layers=1, batch=4, lens=(37, 128, 255, 512), dtype=F16, min_blocks=256, graph=True),
     "attn": Workload(
         "attn", "KV append + paged decode attention HBM GB/s (decode step, Llama-3.1-8B shape)",
         "decode step with attention reading the pool in place: 32 layers x 8 KV heads x 128, block 16, bf16, "
@@ -684,6 +685,9 @@ def config_of(w, H, num_blocks, world):
     if w.bits:
         c.update({"quant_bits": w.bits, "group_size": w.group, "meta": "f16" if w.meta == F16 else "f32",
                   "outliers": w.outliers})
+    if w.graph:
+        c["launch"] = ("device-timed steps replayed from one CUDA graph of the K steps' library launches; "
+                       "the e2e loop calls the C ABI per step")
     return c
 
 
@@ -821,13 +825,15 @@ def main():
         out_v = torch.empty_like(out_k)
     ls = B * H * D
 
-    def launch_step(s, ev_pair=None):
+    def launch_step(s, ev_pair=None, sp=sp, gathers_only=False):
         """The append, then the gather of every layer.  ev_pair brackets the
         step's gathers (not each launch: events between launches would stop
         consecutive kernels from overlapping their launch with the tail of
         the previous one)."""
-        rc = lib.rmlx_kv_append(h, 0, L, new_k[s].data_ptr(), new_v[s].data_ptr(), ls, ts, hs,
-                                slots_d[s].data_ptr(), B, sp)
+        rc = 0
+        if not gathers_only:
+            rc = lib.rmlx_kv_append(h, 0, L, new_k[s].data_ptr(), new_v[s].data_ptr(), ls, ts, hs,
+                                    slots_d[s].data_ptr(), B, sp)
         if ev_pair is not None:
             ev_pair[0].record(stream)
         for layer in range(L):
@@ -863,17 +869,42 @@ def main():
     clocks.start()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if w.graph:
+        # Latency-bound steps: issuing them from Python leaves the GPU idle
+        # between launches, so the K steps' library launches are captured
+        # once (same arguments as the loop below would pass) and replayed.
+        g_steps, g_gathers = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_steps, capture_error_mode="relaxed"):
+            cap = torch.cuda.current_stream().cuda_stream
+            for i in range(K):
+                rc |= launch_step(W + i, sp=cap)
+        with torch.cuda.graph(g_gathers, capture_error_mode="relaxed"):
+            cap = torch.cuda.current_stream().cuda_stream
+            for i in range(K):
+                rc |= launch_step(W + i, sp=cap, gathers_only=True)
+        torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
     e0.record(stream)
-    for i in range(K):
-        rc |= launch_step(W + i, ev[i])
+    if w.graph:
+        g_steps.replay()
+    else:
+        for i in range(K):
+            rc |= launch_step(W + i, ev[i])
     e1.record(stream)
     torch.cuda.synchronize()
     barrier()
     elapsed_ms = max_over_ranks(e0.elapsed_time(e1))
-    # average gather launch = a step's gather span / its L launches
-    gather_ms = [ev[i][0].elapsed_time(ev[i][1]) / L for i in range(K)]
+    if w.graph:
+        # the gather launch time: the K steps' gathers alone, replayed after them
+        ev[0][0].record(stream)
+        g_gathers.replay()
+        ev[0][1].record(stream)
+        torch.cuda.synchronize()
+        gather_ms = [ev[0][0].elapsed_time(ev[0][1]) / (K * L)]
+    else:
+        # average gather launch = a step's gather span / its L launches
+        gather_ms = [ev[i][0].elapsed_time(ev[i][1]) / L for i in range(K)]
     if rc or pool.check() != 0:
         raise SystemExit("launch or device-side validation error in the timed region")
 
