@@ -1661,8 +1661,6 @@ rmlx_status rmlx_kv_decode_attention(rmlx_kv_pool* p, int32_t layer, const void*
   cudaStream_t st = (cudaStream_t)stream;
   const bool bf = c.dtype == RMLX_BF16;
   const int bits = c.quant_bits;
-  const AttnPlan plan = attn_plan(p, num_seqs, G);
-  AttnFn fa = plan.fn;
   CombineFn fc = hd == 128 ? (bf ? attn_combine_kernel<RMLX_BF16, 128> : attn_combine_kernel<RMLX_F16, 128>)
                            : (bf ? attn_combine_kernel<RMLX_BF16, 64> : attn_combine_kernel<RMLX_F16, 64>);
   if (!p->attn_work) {  // the item counter: pool memory, zero between launches
@@ -1673,12 +1671,22 @@ rmlx_status rmlx_kv_decode_attention(rmlx_kv_pool* p, int32_t layer, const void*
     }
     p->attn_work = static_cast<unsigned long long*>(w);
   }
-  const size_t smem = plan.smem;
-  if (smem > 227 * 1024) return fail(RMLX_E_BAD_ARG, "num_seqs too large for one decode attention launch");
   rmlx_status s;
-  if ((s = prepare_smem(fa, smem)) != RMLX_OK) return s;
-  const int grid = persistent_grid(fa, ATT_WARPS * 32, smem, p->num_sms);
-  const int64_t target = attn_target(fa, smem, p->num_sms, plan.items_x2);
+  if (p->attn_nseq != num_seqs || p->attn_G != G) {  // the launch shape, kept for the next call with the same shape
+    const AttnPlan plan = attn_plan(p, num_seqs, G);
+    if (plan.smem > 227 * 1024) return fail(RMLX_E_BAD_ARG, "num_seqs too large for one decode attention launch");
+    if ((s = prepare_smem(plan.fn, plan.smem)) != RMLX_OK) return s;
+    p->attn_fn = reinterpret_cast<void*>(plan.fn);
+    p->attn_smem = plan.smem;
+    p->attn_grid = persistent_grid(plan.fn, ATT_WARPS * 32, plan.smem, p->num_sms);
+    p->attn_target = attn_target(plan.fn, plan.smem, p->num_sms, plan.items_x2);
+    p->attn_nseq = num_seqs;
+    p->attn_G = G;
+  }
+  AttnFn fa = reinterpret_cast<AttnFn>(p->attn_fn);
+  const size_t smem = p->attn_smem;
+  const int grid = p->attn_grid;
+  const int64_t target = p->attn_target;
   const float scale_log2 = softmax_scale * 1.4426950408889634f;  // log2(e)
   cudaError_t e = launch_pdl(fa, dim3(grid), dim3(ATT_WARPS * 32), smem, st, p->geo(), (int)layer,
                              static_cast<const uint8_t*>(q), G, block_tables, (int)block_table_stride, seq_lens,

@@ -101,6 +101,12 @@ struct rmlx_kv_pool {
   int gather_grid = 0;
   // Work-item counter of the decode attention (zero between launches).
   unsigned long long* attn_work = nullptr;
+  // The decode attention's launch shape for the last (num_seqs, q_heads_per_kv):
+  // split kernel, its dynamic shared memory, grid and work-item target.
+  int attn_nseq = -1, attn_G = -1, attn_grid = 0;
+  void* attn_fn = nullptr;
+  size_t attn_smem = 0;
+  int64_t attn_target = 0;
   rmlx::PoolGeo geo() const {
     rmlx::PoolGeo g;
     g.base = base;
