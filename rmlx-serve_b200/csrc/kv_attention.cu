@@ -123,9 +123,13 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
 // elements of the 16 partial outputs, all loaded before any arithmetic, so a
 // round costs one memory latency; weights reach the lanes by shuffle and an
 // online max carries across rounds.
-template <int DT, int HD>
-__device__ __forceinline__ void combine_splits(const float* part_o, const float* part_ml, uint8_t* out, int s,
-                                               int h, int j, int G, int heads, int base, int n, int lane) {
+template <int HD>
+__device__ __forceinline__ void merge_splits(const float* part_o, const float* part_ml, int h, int j, int G,
+                                             int heads, int base, int k0, int kstep, int nk, int lane, float& mx,
+                                             float& L, float* acc) {
+  // splits base + k0 + t * kstep, t < nk, into the running (mx, L, acc);
+  // L is held as per-lane shares (each lane's own splits), acc as this
+  // lane's head_dim / 32 elements
   constexpr int EPL = HD / 32;
   constexpr int R = 16;
   constexpr unsigned FULL = 0xffffffffu;
@@ -133,17 +137,14 @@ __device__ __forceinline__ void combine_splits(const float* part_o, const float*
   const int64_t mstride = (int64_t)heads * G;
   const float* po = part_o + (((int64_t)base * heads + h) * G + j) * HD + lane * EPL;
   const int64_t ostride = (int64_t)heads * G * HD;
-  float mx = -INFINITY, L = 0.0f, acc[EPL];
-#pragma unroll
-  for (int e = 0; e < EPL; ++e) acc[e] = 0.0f;
-  for (int r0 = 0; r0 < n; r0 += R) {
-    const int cnt = min(R, n - r0);
+  for (int r0 = 0; r0 < nk; r0 += R) {
+    const int cnt = min(R, nk - r0);
     float2 mlv = make_float2(-INFINITY, 0.0f);
-    if (lane < cnt) mlv = __ldcg(ml + (int64_t)(r0 + lane) * mstride);
+    if (lane < cnt) mlv = __ldcg(ml + (int64_t)(k0 + (r0 + lane) * kstep) * mstride);
     float vv[R][EPL];
 #pragma unroll
     for (int k = 0; k < R; ++k) {
-      const float* pk = po + (int64_t)(r0 + k) * ostride;
+      const float* pk = po + (int64_t)(k0 + (r0 + k) * kstep) * ostride;
 #pragma unroll
       for (int e = 0; e < EPL; e += 2) {
         float2 x = make_float2(0.0f, 0.0f);
@@ -170,15 +171,32 @@ __device__ __forceinline__ void combine_splits(const float* part_o, const float*
       for (int e = 0; e < EPL; ++e) acc[e] += w * vv[k][e];
     }
   }
-#pragma unroll
-  for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(FULL, L, o);
-  const float inv = 1.0f / L;
+}
+
+template <int DT, int HD>
+__device__ __forceinline__ void store_out_row(uint8_t* out, int s, int h, int j, int G, int heads, const float* acc,
+                                              float inv, int lane) {
+  constexpr int EPL = HD / 32;
   uint32_t wv[EPL / 2];
 #pragma unroll
   for (int e = 0; e < EPL; e += 2) wv[e / 2] = pack2<DT>(acc[e] * inv, acc[e + 1] * inv);
   uint8_t* dst = out + ((int64_t)s * heads * G + (int64_t)h * G + j) * HD * 2 + lane * EPL * 2;
   if (EPL == 4) *reinterpret_cast<uint2*>(dst) = make_uint2(wv[0], wv[1]);
   else *reinterpret_cast<uint32_t*>(dst) = wv[0];
+}
+
+template <int DT, int HD>
+__device__ __forceinline__ void combine_splits(const float* part_o, const float* part_ml, uint8_t* out, int s,
+                                               int h, int j, int G, int heads, int base, int n, int lane) {
+  constexpr int EPL = HD / 32;
+  constexpr unsigned FULL = 0xffffffffu;
+  float mx = -INFINITY, L = 0.0f, acc[EPL];
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) acc[e] = 0.0f;
+  merge_splits<HD>(part_o, part_ml, h, j, G, heads, base, 0, 1, n, lane, mx, L, acc);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(FULL, L, o);
+  store_out_row<DT, HD>(out, s, h, j, G, heads, acc, 1.0f / L, lane);
 }
 
 // Split size of a launch: 256 tokens, halved (down to 64) while the launch
@@ -1478,6 +1496,73 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const int32_t* __rest
   }
 }
 
+// The same combine for launches with few (sequence, query head) pairs and
+// many splits each (a KV-head shard of a few heads): one CTA per pair, its
+// 8 warps merging every 8th split each (one memory round trip for up to 128
+// splits), then the 8 partial (max, sum, output) in shared memory merged by
+// warp 0.
+template <int DT, int HD>
+__global__ void __launch_bounds__(256) attn_combine_cta_kernel(const int32_t* __restrict__ lens, int nseq,
+                                                               int64_t target, int heads, int G,
+                                                               const float* __restrict__ part_o,
+                                                               const float* __restrict__ part_ml,
+                                                               uint8_t* __restrict__ out, int64_t cap_splits,
+                                                               unsigned long long* __restrict__ work) {
+  constexpr int EPL = HD / 32, NW = 8;
+  constexpr unsigned FULL = 0xffffffffu;
+  extern __shared__ int32_t cs[];
+  int32_t* cub = cs;
+  int32_t* cut = cs + nseq + 1;
+  float* red = reinterpret_cast<float*>(cs + ((2 * (nseq + 1) + 3) & ~3));  // [NW][2 + HD]: max, sum, output
+  pdl_release();
+  pick_split(lens, nseq, heads, target, cap_splits, cub, cut);
+  pdl_wait();
+  if (blockIdx.x == 0 && threadIdx.x == 0) *work = 0;  // the split kernel has taken all its items
+  if (cub[nseq] > cap_splits) return;  // flagged by the split kernel
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qheads = heads * G;
+  const int64_t total = (int64_t)nseq * qheads;
+  for (int64_t pr = blockIdx.x; pr < total; pr += gridDim.x) {
+    const int s = (int)(pr / qheads), qh = (int)(pr % qheads);
+    const int n = cub[s + 1] - cub[s];
+    if (n < 2) continue;  // the split kernel wrote it
+    const int h = qh / G, j = qh % G;
+    float mx = -INFINITY, L = 0.0f, acc[EPL];
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) acc[e] = 0.0f;
+    const int nk = warp < n ? (n - warp + NW - 1) / NW : 0;
+    merge_splits<HD>(part_o, part_ml, h, j, G, heads, cub[s], warp, NW, nk, lane, mx, L, acc);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(FULL, L, o);
+    float* rw = red + warp * (2 + HD);
+    if (lane == 0) {
+      rw[0] = mx;
+      rw[1] = L;
+    }
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) rw[2 + lane * EPL + e] = acc[e];
+    __syncthreads();
+    if (warp == 0) {
+      float m = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < NW; ++w) m = fmaxf(m, red[w * (2 + HD)]);  // finite: n >= 2 splits
+      float lt = 0.0f, o[EPL];
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) o[e] = 0.0f;
+#pragma unroll
+      for (int w = 0; w < NW; ++w) {
+        const float* r = red + w * (2 + HD);
+        const float a = ex2(r[0] - m);  // 0 for a warp without splits (max -inf)
+        lt += a * r[1];
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) o[e] += a * r[2 + lane * EPL + e];
+      }
+      store_out_row<DT, HD>(out, s, h, j, G, heads, o, 1.0f / lt, lane);
+    }
+    __syncthreads();  // red is reused by the next pair
+  }
+}
+
 }  // namespace rmlx
 
 using namespace rmlx;
@@ -1661,8 +1746,15 @@ rmlx_status rmlx_kv_decode_attention(rmlx_kv_pool* p, int32_t layer, const void*
   cudaStream_t st = (cudaStream_t)stream;
   const bool bf = c.dtype == RMLX_BF16;
   const int bits = c.quant_bits;
-  CombineFn fc = hd == 128 ? (bf ? attn_combine_kernel<RMLX_BF16, 128> : attn_combine_kernel<RMLX_F16, 128>)
-                           : (bf ? attn_combine_kernel<RMLX_BF16, 64> : attn_combine_kernel<RMLX_F16, 64>);
+  // one warp per (sequence, query head); with fewer pairs than warps of
+  // one CTA per SM, one CTA per pair (its warps share the pair's splits)
+  const int64_t pairs = (int64_t)num_seqs * heads * G;
+  const bool cta_combine = pairs < (int64_t)p->num_sms * 8;
+  CombineFn fc = cta_combine
+                     ? (hd == 128 ? (bf ? attn_combine_cta_kernel<RMLX_BF16, 128> : attn_combine_cta_kernel<RMLX_F16, 128>)
+                                  : (bf ? attn_combine_cta_kernel<RMLX_BF16, 64> : attn_combine_cta_kernel<RMLX_F16, 64>))
+                     : (hd == 128 ? (bf ? attn_combine_kernel<RMLX_BF16, 128> : attn_combine_kernel<RMLX_F16, 128>)
+                                  : (bf ? attn_combine_kernel<RMLX_BF16, 64> : attn_combine_kernel<RMLX_F16, 64>));
   if (!p->attn_work) {  // the item counter: pool memory, zero between launches
     void* w = nullptr;
     if (cudaMalloc(&w, 16) != cudaSuccess || cudaMemset(w, 0, 16) != cudaSuccess) {
@@ -1693,10 +1785,10 @@ rmlx_status rmlx_kv_decode_attention(rmlx_kv_pool* p, int32_t layer, const void*
                              (int)num_seqs, target, scale_log2, part_o, part_ml, cap, static_cast<uint8_t*>(out),
                              bits ? log2i(c.group_size) : 0, p->attn_work, p->err);
   if (e != cudaSuccess) return cuda_check(e, "decode attention launch");
-  const size_t csmem = (size_t)2 * (num_seqs + 1) * 4;
+  const size_t csmem = cta_combine ? (size_t)((2 * (num_seqs + 1) + 3) & ~3) * 4 + (size_t)8 * (2 + hd) * 4
+                                   : (size_t)2 * (num_seqs + 1) * 4;
   if ((s = prepare_smem(fc, csmem)) != RMLX_OK) return s;
-  const int64_t warps = (int64_t)num_seqs * heads * G;
-  const int cgrid = (int)std::min<int64_t>((warps + 7) / 8, (int64_t)p->num_sms * 8);
+  const int cgrid = cta_combine ? (int)pairs : (int)std::min<int64_t>((pairs + 7) / 8, (int64_t)p->num_sms * 8);
   e = launch_pdl(fc, dim3(cgrid), dim3(256), csmem, st, seq_lens, (int)num_seqs, target, heads, G, part_o,
                  part_ml, static_cast<uint8_t*>(out), cap, p->attn_work);
   if (e != cudaSuccess) {
