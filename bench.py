@@ -936,7 +936,11 @@ def main():
     # slot, new blocks and block tables; H2D of the new K/V (pinned), slots,
     # block tables and lengths; the append and the per-layer gathers (or
     # attention); a D2H read of the step's status word.  The gathered K/V stay
-    # in HBM for the attention that consumes them.
+    # in HBM for the attention that consumes them.  Inputs are double-
+    # buffered: step i + 1's copies run on a copy stream while step i
+    # computes, and each step's status word is read asynchronously
+    # (rmlx_kv_pool_status_async) and checked on the host two steps later,
+    # when its buffers are reused.
     from rmlx_kv.batch import KVBatch
     mgr = rmlx_kv.PagedCacheManager(BS, num_blocks)
     rng = np.random.default_rng(w.seed + 7)
@@ -951,50 +955,76 @@ def main():
     pin_v = torch.empty_like(pin_k, pin_memory=True)
     pin_k.copy_(new_k[W:W + K].cpu())
     pin_v.copy_(new_v[W:W + K].cpu())
-    pin_bt = torch.from_numpy(host_bt).pin_memory()
-    pin_slots = torch.empty(B, dtype=torch.int32, pin_memory=True)
-    pin_lens = torch.empty(B, dtype=torch.int32, pin_memory=True)
-    dk = torch.empty((L, B, H, D), device="cuda", dtype=tdt)
-    dv = torch.empty_like(dk)
-    d_slots = torch.empty(B, dtype=torch.int32, device="cuda")
-    d_lens = torch.empty(B, dtype=torch.int32, device="cuda")
-    d_bt = torch.empty_like(bt_d)
-    h2d = 2 * dk.numel() * 2 + 2 * B * 4 + host_bt.nbytes
+    # two sets of host (pinned) and device buffers, used by alternate steps
+    pin_bt = [torch.from_numpy(host_bt.copy()).pin_memory() for _ in range(2)]
+    pin_slots = [torch.empty(B, dtype=torch.int32, pin_memory=True) for _ in range(2)]
+    pin_lens = [torch.empty(B, dtype=torch.int32, pin_memory=True) for _ in range(2)]
+    pin_status = [torch.zeros(1, dtype=torch.int32, pin_memory=True) for _ in range(2)]
+    dk = [torch.empty((L, B, H, D), device="cuda", dtype=tdt) for _ in range(2)]
+    dv = [torch.empty_like(dk[0]) for _ in range(2)]
+    d_slots = [torch.empty(B, dtype=torch.int32, device="cuda") for _ in range(2)]
+    d_lens = [torch.empty(B, dtype=torch.int32, device="cuda") for _ in range(2)]
+    d_bt = [torch.empty_like(bt_d) for _ in range(2)]
+    h2d = 2 * dk[0].numel() * 2 + 2 * B * 4 + host_bt.nbytes
     if G:
         # the step's queries for every layer come from the host too
         pin_q = q_d.cpu().pin_memory()
-        dq = torch.empty_like(q_d)
+        dq = [torch.empty_like(q_d) for _ in range(2)]
         h2d += q_d.numel() * 2
+    copy_stream = torch.cuda.Stream()
+    copied = [torch.cuda.Event() for _ in range(2)]
+    done = [torch.cuda.Event() for _ in range(2)]
+
+    def status_seen(b):
+        """The status word of the step that last used buffer set b (its
+        event has completed)."""
+        done[b].synchronize()
+        return int(pin_status[b][0])
+
     barrier()
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     for i in range(K):
+        b = i % 2
         slots_i, _, _ = planner.step(uids, step_tokens[i])
         tb, ln = planner.tables()
-        pin_slots.numpy()[:] = slots_i
-        pin_lens.numpy()[:] = ln
-        pin_bt.numpy()[:, :tb.shape[1]] = tb
-        dk.copy_(pin_k[i], non_blocking=True)
-        dv.copy_(pin_v[i], non_blocking=True)
-        d_slots.copy_(pin_slots, non_blocking=True)
-        d_lens.copy_(pin_lens, non_blocking=True)
-        d_bt.copy_(pin_bt, non_blocking=True)
-        rc |= lib.rmlx_kv_append(h, 0, L, dk.data_ptr(), dv.data_ptr(), ls, ts, hs, d_slots.data_ptr(), B, sp)
-        if G:
-            dq.copy_(pin_q, non_blocking=True)
+        if i >= 2 and status_seen(b):  # step i - 2 finished with set b: its status word
+            raise SystemExit("device-side validation error in the e2e loop")
+        pin_slots[b].numpy()[:] = slots_i
+        pin_lens[b].numpy()[:] = ln
+        pin_bt[b].numpy()[:, :tb.shape[1]] = tb
+        with torch.cuda.stream(copy_stream):
+            dk[b].copy_(pin_k[i], non_blocking=True)
+            dv[b].copy_(pin_v[i], non_blocking=True)
+            d_slots[b].copy_(pin_slots[b], non_blocking=True)
+            d_lens[b].copy_(pin_lens[b], non_blocking=True)
+            d_bt[b].copy_(pin_bt[b], non_blocking=True)
+            if G:
+                dq[b].copy_(pin_q, non_blocking=True)
+            copied[b].record(copy_stream)
+        stream.wait_event(copied[b])
+        rc |= lib.rmlx_kv_append(h, 0, L, dk[b].data_ptr(), dv[b].data_ptr(), ls, ts, hs, d_slots[b].data_ptr(), B,
+                                 sp)
         for layer in range(L):
             if G:
-                rc |= lib.rmlx_kv_decode_attention(h, layer, dq[layer].data_ptr(), G, d_bt.data_ptr(), bt.shape[1],
-                                                   d_lens.data_ptr(), B, scale, att_out.data_ptr(), ws.data_ptr(),
-                                                   ws_bytes, sp)
+                rc |= lib.rmlx_kv_decode_attention(h, layer, dq[b][layer].data_ptr(), G, d_bt[b].data_ptr(),
+                                                   bt.shape[1], d_lens[b].data_ptr(), B, scale, att_out.data_ptr(),
+                                                   ws.data_ptr(), ws_bytes, sp)
             else:
-                rc |= lib.rmlx_kv_gather(h, layer, d_bt.data_ptr(), bt.shape[1], d_lens.data_ptr(), B,
+                rc |= lib.rmlx_kv_gather(h, layer, d_bt[b].data_ptr(), bt.shape[1], d_lens[b].data_ptr(), B,
                                          out_k.data_ptr(), out_v.data_ptr(), sp)
-        if rc or pool.check():  # the step's status word, read back to the host
-            raise SystemExit("launch or device-side validation error in the e2e loop")
+        # the step's status word, read back to the host without waiting
+        rc |= lib.rmlx_kv_pool_status_async(h, pin_status[b].data_ptr(), sp)
+        done[b].record(stream)
+        if rc:
+            raise SystemExit("launch error in the e2e loop")
+    if any(status_seen(b) for b in range(min(K, 2))):
+        raise SystemExit("device-side validation error in the e2e loop")
     torch.cuda.synchronize()
     barrier()
     e2e_s = max_over_ranks(time.perf_counter() - t0)
+    if pool.check():
+        raise SystemExit("device-side validation error in the e2e loop")
     clk = clocks.stop()
     e2e_value = tot_bytes / e2e_s / 1e9
 

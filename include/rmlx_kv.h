@@ -297,6 +297,13 @@ RMLX_API void rmlx_kv_pool_destroy(rmlx_kv_pool* p);
 RMLX_API rmlx_status rmlx_kv_pool_layout(const rmlx_kv_pool* p, rmlx_pool_layout* out);
 /* Reads and clears the device error word (synchronises the pool's device). */
 RMLX_API rmlx_status rmlx_kv_pool_check(rmlx_kv_pool* p, int32_t* device_error);
+/* Copies the device error word into *status on `stream` without waiting for
+ * it and without clearing it: the value is valid once the stream has passed
+ * this point (an event recorded after it, say).  For a serving loop that
+ * reads each step's status without stalling the next step's launches; pass
+ * pinned host memory, or the copy is not asynchronous.  No counterpart in
+ * the reference crate, whose errors are synchronous panics. */
+RMLX_API rmlx_status rmlx_kv_pool_status_async(rmlx_kv_pool* p, int32_t* status, void* stream);
 
 /* Synchronous copies between host memory and pool bytes
  * [offset, offset + nbytes) (raw byte images of the pool; the prompt-cache

@@ -822,6 +822,14 @@ rmlx_status rmlx_kv_pool_check(rmlx_kv_pool* p, int32_t* device_error) {
   return cuda_check(cudaMemset(p->err, 0, sizeof(int32_t)), "clear error word");
 }
 
+rmlx_status rmlx_kv_pool_status_async(rmlx_kv_pool* p, int32_t* status, void* stream) {
+  if (!p || !status) return fail(RMLX_E_BAD_ARG, "NULL pool or status");
+  DeviceGuard dg(p->device);
+  return cuda_check(
+      cudaMemcpyAsync(status, p->err, sizeof(int32_t), cudaMemcpyDeviceToHost, (cudaStream_t)stream),
+      "read error word");
+}
+
 rmlx_status rmlx_kv_pool_read(rmlx_kv_pool* p, size_t offset, size_t nbytes, void* host_dst) {
   if (!p || (nbytes && !host_dst)) return fail(RMLX_E_BAD_ARG, "NULL pool or destination");
   if (offset > p->bytes || nbytes > p->bytes - offset) return fail(RMLX_E_RANGE, "read past the end of the pool");

@@ -149,6 +149,7 @@ _sig("rmlx_kv_pool_new", st, C.POINTER(PoolConfig), C.c_int, C.POINTER(vp))
 _sig("rmlx_kv_pool_destroy", None, vp)
 _sig("rmlx_kv_pool_layout", st, vp, C.POINTER(PoolLayout))
 _sig("rmlx_kv_pool_check", st, vp, i32p)
+_sig("rmlx_kv_pool_status_async", st, vp, vp, vp)
 _sig("rmlx_kv_pool_read", st, vp, C.c_size_t, C.c_size_t, vp)
 _sig("rmlx_kv_pool_write", st, vp, C.c_size_t, C.c_size_t, vp)
 _sig("rmlx_kv_append", st, vp, C.c_int32, C.c_int32, vp, vp, C.c_int64, C.c_int64, C.c_int64, vp,

@@ -147,6 +147,36 @@ def test_out_of_pool_ids_are_flagged_not_written(cuda):
     np.testing.assert_array_equal(to_host(out, np.uint16), ek)
 
 
+def test_status_async_reads_without_clearing(cuda):
+    """rmlx_kv_pool_status_async copies the error word on a stream without
+    waiting and without clearing it: 0 on a clean pool, the latched bit after
+    an out-of-pool slot (once an event after it has completed), and the word
+    is still there for the synchronous check, which clears it."""
+    import torch
+    from rmlx_kv import _lib
+    L, H, D, bs, N = 1, 1, 64, 4, 4
+    pool = rmlx_kv.KVPool(L, H, D, bs, N, dtype=orc.BF16)
+    stream = torch.cuda.current_stream()
+    word = torch.full((1,), -1, dtype=torch.int32).pin_memory()
+
+    def read_async():
+        _lib.check(_lib.lib.rmlx_kv_pool_status_async(pool.handle, word.data_ptr(), stream.cuda_stream))
+        ev = torch.cuda.Event()
+        ev.record(stream)
+        ev.synchronize()
+        return int(word[0])
+
+    assert read_async() == 0
+    k = rand_rows(np.random.default_rng(9), (L, 1, H, D), orc.BF16)
+    pool.append(to_dev(k), to_dev(k), to_dev(np.array([N * bs], dtype=np.int32)), 1)
+    assert read_async() & 1  # DEV_ERR_SLOT
+    assert read_async() & 1  # not cleared by the asynchronous read
+    assert pool.check() & 1
+    assert read_async() == 0
+    assert _lib.lib.rmlx_kv_pool_status_async(pool.handle, None, stream.cuda_stream) == _lib.RMLX_E_BAD_ARG
+    pool.close()
+
+
 def test_bad_arguments_rejected(cuda):
     with pytest.raises(rmlx_kv.RmlxError):
         rmlx_kv.KVPool(1, 1, 12, 16, 4, dtype=orc.BF16)  # 24-byte rows are not 16-byte multiples
