@@ -6,23 +6,33 @@
 // len tokens, K/V rows located through the block table exactly like the
 // gather (token t: block bt[s][t / block_size], row t % block_size).
 //
-// Split over the sequence (flash-decoding): a work item is (split of 256
-// tokens, KV head), one warp per item.  A warp streams its split in chunks of
-// 16 tokens through shared memory (cp.async, two stages per warp) and runs
-// both products on the tensor cores with mma.sync m16n8k16 (f16/bf16 inputs,
-// f32 accumulation): S = Q K^T with the G query heads as the M rows, then
-// O += P V with P (the exponentiated scores, rounded to the pool's type) as
-// the A operand.  An online softmax in the log2 domain keeps a running max
-// and sum per query head.  A sequence held by one item is normalised and
-// written directly; otherwise each item writes its unnormalised O, max and
-// sum to a workspace, and a second kernel combines the splits of each
+// Split over the sequence (flash-decoding): a work item is (split of 256,
+// 128 or 64 tokens, KV head), one warp per item, items handed out by a
+// counter.  A warp streams its split in chunks of 16 tokens through shared
+// memory (cp.async) and runs both products on the tensor cores with
+// mma.sync m16n8k16 (f16/bf16 inputs, f32 accumulation), with an online
+// softmax in the log2 domain.  A sequence held by one item is normalised
+// and written directly; otherwise each item writes its unnormalised O, max
+// and sum to a workspace, and a second kernel combines the splits of each
 // (sequence, query head) and writes the output in the pool's type.
 //
-// The kernel is HBM-bound: per token and KV head it reads 2 x head_dim x 2
-// bytes and does 4 x G x head_dim flops (G = 4..8: 8..16 flops per byte),
-// two orders of magnitude under the tensor cores' ridge point, so the legacy
-// warp-level mma is not the limit; what matters is that every K/V byte is
-// read once with enough bytes in flight.
+// Three split kernels:
+//   * paged_decode_attn_rows_kernel (bf16/f16 pools): tokens are the M rows
+//     and the query heads the N columns of both products (S^T = K Q^T,
+//     O^T += V^T P^T), the queries held in registers;
+//   * paged_decode_attn_codes_kernel (quantised pools whose groups span
+//     whole k-steps): the same orientation, fed the 4/8-bit codes as exact
+//     f16 integers, with scale and zero applied around the products;
+//   * paged_decode_attn_kernel (quantised pools with smaller groups): the
+//     query heads as the M rows, K and V dequantised into a shared-memory
+//     tile first.
+//
+// The work is HBM-bound by arithmetic intensity: per token and KV head a
+// bf16 pool reads 2 x head_dim x 2 bytes for 4 x G x head_dim flops (G =
+// 4..8: 8..16 flops per byte), two orders of magnitude under the tensor
+// cores' ridge point, so the warp-level mma is not the limit; what matters
+// is that every K/V byte is read once with enough bytes in flight, and, for
+// quantised pools, how few instructions each code costs.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
