@@ -6,8 +6,8 @@
 // len tokens, K/V rows located through the block table exactly like the
 // gather (token t: block bt[s][t / block_size], row t % block_size).
 //
-// Split over the sequence (flash-decoding): a work item is (split of 256,
-// 128 or 64 tokens, KV head), one warp per item, items handed out by a
+// Split over the sequence (flash-decoding): a work item is (split of 256
+// down to 64 tokens, KV head), one warp per item, items handed out by a
 // counter.  A warp streams its split in chunks of 16 tokens through shared
 // memory (cp.async) and runs both products on the tensor cores with
 // mma.sync m16n8k16 (f16/bf16 inputs, f32 accumulation), with an online
@@ -1714,8 +1714,8 @@ rmlx_status rmlx_kv_attention_workspace_size(const rmlx_kv_pool* p, int32_t q_he
   const rmlx_pool_config& c = p->cfg;
   int64_t splits = max_total_tokens / ATT_SPLIT + num_seqs;
   if ((c.dtype == RMLX_F16 || c.dtype == RMLX_BF16) && (c.head_dim == 64 || c.head_dim == 128)) {
-    // room for the smaller splits a launch with few work items takes (down
-    // to 64 tokens: at most 4x the splits of a launch below the target)
+    // room for the smaller splits a launch with few work items takes: the
+    // last halving starts below the target, so at most twice it (4x kept)
     const AttnPlan plan = attn_plan(p, num_seqs, q_heads_per_kv);
     DeviceGuard dg(p->device);
     if (plan.smem <= 227 * 1024 && prepare_smem(plan.fn, plan.smem) == RMLX_OK) {
