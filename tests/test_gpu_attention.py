@@ -243,10 +243,12 @@ def test_quantised_pool(cuda, bits, meta):
 
 
 @pytest.mark.parametrize("bs,D,gs,dt", [(8, 128, 32, orc.BF16), (1, 64, 16, orc.F16), (32, 64, 64, orc.F16),
-                                        (5, 128, 128, orc.BF16)])
+                                        (5, 128, 128, orc.BF16), (16, 128, 8, orc.BF16)])
 def test_quantised_block_sizes_and_groups(cuda, bs, D, gs, dt):
     """bs 8, 1 and 5: chunks span blocks (row-by-row copies of codes and of
-    4-, 8- or 16-byte scale/zero rows); 32: two chunks per block."""
+    4-, 8- or 16-byte scale/zero rows); 32: two chunks per block.  Groups of
+    8 (both widths) and of 16 at 4 bits are below what the codes kernel
+    takes: the kernel that dequantises into a tile serves them."""
     N = 700 // bs + 40
     for bits in (8, 4):
         run_attn_quant(cuda, 1, 2, D, bs, N, dt, 8, [3, 16, 31, 300], 80 + bs + bits, bits, gs, orc.F16)
