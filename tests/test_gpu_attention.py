@@ -193,7 +193,7 @@ def run_attn_quant(cuda, L, H, D, bs, N, dt, G, lens, seed, bits, gs, meta, laye
     one.  The tolerances grow with the largest |V|, and the RMS bound also
     allows for the output's own rounding to the pool's type."""
     import torch
-    from helpers import rand_rows, slots_for
+    from helpers import slots_for
     rng = np.random.default_rng(seed)
     pool = rmlx_kv.KVPool(L, H, D, bs, N, dtype=dt, quant_bits=bits, group_size=gs, meta_dtype=meta)
     pool.write(np.zeros(pool.layout.bytes, np.uint8))

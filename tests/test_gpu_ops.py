@@ -6,7 +6,7 @@ import pytest
 
 import oracle as orc
 import rmlx_kv
-from helpers import rand_rows, to_dev
+from helpers import to_dev
 
 pytestmark = pytest.mark.gpu
 
