@@ -1756,10 +1756,12 @@ rmlx_status rmlx_kv_decode_attention(rmlx_kv_pool* p, int32_t layer, const void*
   cudaStream_t st = (cudaStream_t)stream;
   const bool bf = c.dtype == RMLX_BF16;
   const int bits = c.quant_bits;
-  // one warp per (sequence, query head); with fewer pairs than warps of
-  // one CTA per SM, one CTA per pair (its warps share the pair's splits)
+  // one warp per (sequence, query head); with few pairs (each with many
+  // splits: a launch over a shard of the KV heads) one CTA per pair, its
+  // warps sharing the pair's splits.  Measured crossover: 512 pairs are
+  // faster per CTA, 1024 per warp.
   const int64_t pairs = (int64_t)num_seqs * heads * G;
-  const bool cta_combine = pairs < (int64_t)p->num_sms * 8;
+  const bool cta_combine = pairs < (int64_t)p->num_sms * 4;
   CombineFn fc = cta_combine
                      ? (hd == 128 ? (bf ? attn_combine_cta_kernel<RMLX_BF16, 128> : attn_combine_cta_kernel<RMLX_F16, 128>)
                                   : (bf ? attn_combine_cta_kernel<RMLX_BF16, 64> : attn_combine_cta_kernel<RMLX_F16, 64>))
