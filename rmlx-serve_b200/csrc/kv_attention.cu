@@ -1591,7 +1591,8 @@ using CombineFn = void (*)(const int32_t*, int, int64_t, int, int, const float*,
 // Work items a launch wants before it halves its split size: items_x2 / 2
 // per resident warp.  Fewer, longer items save per-item work (queries,
 // partials, combine); more items even out the tail.  Measured per kernel:
-// 1.5 for the bf16/f16 and 8-bit kernels, 3 for the 4-bit one.
+// 1 for the bf16/f16 kernel, 1.5 for the 8-bit codes kernel, 3 for the 4-bit
+// one.
 int64_t attn_target(AttnFn fa, size_t smem, int num_sms, int items_x2) {
   return (int64_t)items_x2 * persistent_grid(fa, ATT_WARPS * 32, smem, num_sms) * ATT_WARPS / 2;
 }
@@ -1697,7 +1698,7 @@ AttnPlan attn_plan(const rmlx_kv_pool* p, int nseq, int G) {
     const bool bf = c.dtype == RMLX_BF16;
     AttnFn fn = hd == 128 ? (bf ? pick_rows<RMLX_BF16, 128>(G) : pick_rows<RMLX_F16, 128>(G))
                           : (bf ? pick_rows<RMLX_BF16, 64>(G) : pick_rows<RMLX_F16, 64>(G));
-    return {fn, attn_rows_smem(nseq, hd), 3};
+    return {fn, attn_rows_smem(nseq, hd), 2};
   }
   return {attn_kernel_of(c),
           attn_smem(nseq, hd, ATT_STAGES, ATT_QSMEM, c.quant_bits, (int)p->row_bytes, (int)p->meta_row_bytes), 6};
