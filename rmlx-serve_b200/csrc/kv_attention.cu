@@ -704,7 +704,10 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
 // 1024 + 64 sum over those riding on 64), and O^T's accumulator starts at
 // sum_t P z / smax - (offset + 2^(bits-1)) sum_t P s / smax, with the weights
 // P s / smax summed as rounded, so that the products see centred codes
-// (code - 2^(bits-1)) and the zeros z + 2^(bits-1) s.
+// (code - 2^(bits-1)) and the zeros z + 2^(bits-1) s.  The two sums that
+// span lanes -- the queries' per-group sums and the rounded weights' per-head
+// sums -- are MMAs against constant A operands (all ones; the offsets), not
+// shuffle reductions.
 //
 // Fragments come straight from the staged code rows (16-byte columns
 // XOR-swizzled, read with ldmatrix):
