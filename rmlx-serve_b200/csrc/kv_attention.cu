@@ -1594,8 +1594,7 @@ using CombineFn = void (*)(const int32_t*, int, int64_t, int, int, const float*,
 // Work items a launch wants before it halves its split size: items_x2 / 2
 // per resident warp.  Fewer, longer items save per-item work (queries,
 // partials, combine); more items even out the tail.  Measured per kernel:
-// 1 for the bf16/f16 kernel, 1.5 for the 8-bit codes kernel, 3 for the 4-bit
-// one.
+// 1 for the bf16/f16 and 8-bit codes kernels, 3 for the 4-bit one.
 int64_t attn_target(AttnFn fa, size_t smem, int num_sms, int items_x2) {
   return (int64_t)items_x2 * persistent_grid(fa, ATT_WARPS * 32, smem, num_sms) * ATT_WARPS / 2;
 }
@@ -1695,7 +1694,7 @@ AttnPlan attn_plan(const rmlx_kv_pool* p, int nseq, int G) {
                           : (G <= 8 ? pick_codes<64, 1>(c) : pick_codes<64, 2>(c));
     if (fn)
       return {fn, attn_codes_smem(nseq, CQ_STAGES, (int)p->row_bytes, (int)p->meta_row_bytes),
-              c.quant_bits == 8 ? 3 : 6};
+              c.quant_bits == 8 ? 2 : 6};
   }
   if (!c.quant_bits) {
     const bool bf = c.dtype == RMLX_BF16;
