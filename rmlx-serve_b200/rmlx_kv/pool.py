@@ -79,6 +79,13 @@ class KVPool:
         check(lib.rmlx_kv_pool_check(self._h, C.byref(e)))
         return e.value
 
+    def status_async(self, word, stream=None) -> None:
+        """Queue a copy of the device error word into `word` (pinned host
+        int32, a torch tensor or an address) on `stream`; nothing waits and
+        the word is not cleared.  Read `word` once an event recorded after
+        this call has completed."""
+        check(lib.rmlx_kv_pool_status_async(self._h, _ptr(word), _stream(stream, self.device)))
+
     def read(self, offset: int = 0, nbytes: Optional[int] = None):
         """Copy pool bytes [offset, offset+nbytes) to a new host numpy array."""
         import numpy as np

@@ -160,7 +160,7 @@ def test_status_async_reads_without_clearing(cuda):
     word = torch.full((1,), -1, dtype=torch.int32).pin_memory()
 
     def read_async():
-        _lib.check(_lib.lib.rmlx_kv_pool_status_async(pool.handle, word.data_ptr(), stream.cuda_stream))
+        pool.status_async(word, stream)
         ev = torch.cuda.Event()
         ev.record(stream)
         ev.synchronize()
