@@ -512,7 +512,12 @@ RMLX_API void rmlx_nccl_comm_destroy(rmlx_comm* c);
 /* Exchange blocks with `peer` (both ranks call it): send blocks send_ids
  * (device array, n_send) of this pool, receive n_recv blocks into recv_ids.
  * Staging buffers are device buffers of n * block_bytes.  Enqueued on
- * `stream`; rmlx_nccl_wait bounds the completion. */
+ * `stream`; rmlx_nccl_wait bounds the completion.
+ * Call it only after both ranks have agreed on the counts on the host, each
+ * confirming that it can hold what comes, with bounded waits (the Python
+ * side's rmlx_kv.distributed.exchange_migration_plan does this through the
+ * process group's key-value store): a rank whose peer has left or failed
+ * must learn it there, not from a transfer posted toward that peer. */
 RMLX_API rmlx_status rmlx_kv_migrate(rmlx_kv_pool* p, rmlx_comm* c, int32_t peer, const int32_t* send_ids,
                                      int32_t n_send, void* send_staging, const int32_t* recv_ids, int32_t n_recv,
                                      void* recv_staging, void* stream);

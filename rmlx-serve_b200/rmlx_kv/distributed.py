@@ -9,13 +9,16 @@ collective.  Two host exchanges remain:
 * agreeing on a migration plan: how many blocks move, and where the
   receiver puts them (it allocates them in its own block manager).
 
-Both run over an existing torch.distributed process group (gloo or NCCL),
-which here is plumbing only; the block bytes move through the library's
-own NCCL communicator (``NcclComm`` / ``KVPool.migrate``).
+The id travels over an existing torch.distributed process group (gloo or
+NCCL); the plan travels through that group's host key-value store with a
+bounded wait, so a rank that has left is found on the host before any
+NCCL transfer is posted toward it.  torch.distributed is plumbing only; the
+block bytes move through the library's own NCCL communicator (``NcclComm``
+/ ``KVPool.migrate``).
 """
 from __future__ import annotations
 
-from typing import List, Tuple
+from typing import List, Optional, Tuple
 
 import numpy as np
 
@@ -49,27 +52,86 @@ def share_nccl_id(group=None) -> bytes:
     return bytes(buf.cpu().numpy().tobytes())
 
 
-def exchange_migration_plan(mgr, send_ids: List[int], peer: int, group=None) -> Tuple[List[int], int]:
+_EPOCH = {}
+
+
+def _default_store():
+    from torch.distributed import distributed_c10d
+    return distributed_c10d._get_default_store()
+
+
+def depart(store=None, rank: Optional[int] = None) -> None:
+    """Announce on the host that this rank leaves the job between steps.
+
+    A rank calls this after its last collective has completed (nothing of
+    its own in flight on the GPU).  A peer's next ``exchange_migration_plan``
+    sees the mark and fails at once with RMLX_E_TIMEOUT instead of waiting
+    out its deadline; it never enqueues an NCCL transfer toward the rank
+    that left."""
+    import torch.distributed as dist
+    store = _default_store() if store is None else store
+    me = dist.get_rank() if rank is None else rank
+    store.set(f"rmlx_kv/departed/{me}", "1")
+
+
+def exchange_migration_plan(mgr, send_ids: List[int], peer: int, group=None, *, store=None,
+                            rank: Optional[int] = None, timeout_s: float = 60.0) -> Tuple[List[int], int]:
     """Tell `peer` how many blocks this rank sends and learn how many it sends
     here; allocate that many destination blocks from `mgr` (this rank's block
-    manager).  Returns (recv_ids, n_peer_sends).  Raises if this pool cannot
-    hold the incoming blocks (nothing is allocated then)."""
-    import torch
+    manager).  Returns (recv_ids, n_peer_sends).
+
+    This is the handshake that must complete before either rank calls
+    ``KVPool.migrate``: it runs entirely on the host, through the key-value
+    store of the process group (or `store`, with `rank` this rank's id), and
+    every wait in it is bounded by `timeout_s`.  A peer that has left
+    (``depart``) or does not answer by the deadline raises ``RmlxError`` with
+    RMLX_E_TIMEOUT before anything is allocated or enqueued, so no NCCL
+    transfer is ever posted toward a rank that will not post its half.
+    Raises RMLX_E_EXHAUSTED, on both ranks, if either pool cannot hold the
+    blocks coming to it (nothing is allocated then).
+
+    Both ranks of a pair call this the same number of times in the same
+    order; the n-th call of each is matched with the n-th call of the other.
+    """
+    import time
     import torch.distributed as dist
-    dev = _dev(group)
-    mine = torch.tensor([len(send_ids)], dtype=torch.int64, device=dev)
-    theirs = torch.zeros(1, dtype=torch.int64, device=dev)
-    me = dist.get_rank()
-    # Deadlock-free pairwise exchange: the lower rank sends first.
-    if me < peer:
-        dist.send(mine, dst=peer, group=group)
-        dist.recv(theirs, src=peer, group=group)
-    else:
-        dist.recv(theirs, src=peer, group=group)
-        dist.send(mine, dst=peer, group=group)
-    n_in = int(theirs.item())
-    if n_in > mgr.num_free_blocks():
-        raise RuntimeError(f"peer sends {n_in} blocks, only {mgr.num_free_blocks()} free here")
+    from ._lib import RMLX_E_EXHAUSTED, RMLX_E_TIMEOUT, RmlxError
+    store = _default_store() if store is None else store
+    me = (dist.get_rank() if group is None else dist.get_global_rank(group, dist.get_rank(group))) \
+        if rank is None else rank
+    if peer == me:
+        raise ValueError("a rank cannot migrate blocks to itself")
+    epoch = _EPOCH.get((me, peer), 0)
+    _EPOCH[(me, peer)] = epoch + 1
+    deadline = time.monotonic() + timeout_s
+
+    def post(phase, value):
+        store.set(f"rmlx_kv/migrate/{me}->{peer}/{epoch}/{phase}", value)
+
+    def hear(phase):
+        key = f"rmlx_kv/migrate/{peer}->{me}/{epoch}/{phase}"
+        while not store.check([key]):
+            if store.check([f"rmlx_kv/departed/{peer}"]):
+                raise RmlxError(RMLX_E_TIMEOUT, f"migration plan: rank {peer} has left the job")
+            if time.monotonic() > deadline:
+                raise RmlxError(RMLX_E_TIMEOUT, f"migration plan: rank {peer} did not answer within {timeout_s:g} s")
+            time.sleep(0.005)
+        v = store.get(key).decode()
+        store.delete_key(key)  # this rank is its only reader
+        return v
+
+    # Phase 1: the block counts.  Phase 2: both sides confirm that they can
+    # take what comes, so that neither posts its transfer while the other
+    # has given up.
+    post("count", str(len(send_ids)))
+    n_in = int(hear("count"))
+    fits = n_in <= mgr.num_free_blocks()
+    post("ready", "1" if fits else "0")
+    peer_ready = hear("ready") == "1"
+    if not fits:
+        raise RmlxError(RMLX_E_EXHAUSTED, f"peer sends {n_in} blocks, only {mgr.num_free_blocks()} free here")
+    if not peer_ready:
+        raise RmlxError(RMLX_E_EXHAUSTED, f"rank {peer} cannot hold the {len(send_ids)} blocks this rank sends")
     recv_ids = mgr.allocate_n(n_in).tolist()
     return recv_ids, n_in
 

@@ -103,3 +103,85 @@ def test_two_rank_host_path():
     assert len(a["recv"]) == 2 and len(b["recv"]) == 5
     assert a["free"] == 64 - 20 - 2 and b["free"] == 64 - 20 - 5
     assert a["bt_changed"] == 5 and b["bt_changed"] == 2
+
+
+def _handshake_worker(rank, world, port, out):
+    """Failure paths of the migration-plan handshake, all on the host."""
+    sys.path.insert(0, os.path.join(ROOT, "rmlx-serve_b200"))
+    import datetime
+    import time
+    import torch.distributed as dist
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    res = {}
+    try:
+        import rmlx_kv
+        from rmlx_kv import _lib
+        from rmlx_kv import distributed as rd
+        # (1) the receiver cannot hold what comes: both ranks fail, neither allocates
+        mgr = rmlx_kv.PagedCacheManager(16, 8 if rank == 1 else 64)
+        mgr.allocate_n(4)
+        free0 = mgr.num_free_blocks()
+        try:
+            rd.exchange_migration_plan(mgr, list(range(6)) if rank == 0 else [0], 1 - rank, timeout_s=30)
+            res["exhausted"] = None
+        except rmlx_kv.RmlxError as e:
+            res["exhausted"] = e.status
+        res["untouched"] = mgr.num_free_blocks() == free0
+        dist.barrier()
+        # (2) a peer that stays up but never answers: the deadline
+        if rank == 0:
+            t0 = time.monotonic()
+            try:
+                rd.exchange_migration_plan(mgr, [1], 1, timeout_s=1.0)
+                res["silent"] = None
+            except rmlx_kv.RmlxError as e:
+                res["silent"] = e.status
+            res["silent_s"] = time.monotonic() - t0
+        dist.barrier()
+        # (3) a peer that leaves between steps: found at once through its mark
+        if rank == 1:
+            rd.depart()
+        dist.barrier()
+        if rank == 0:
+            t0 = time.monotonic()
+            try:
+                rd.exchange_migration_plan(mgr, [1], 1, timeout_s=30)
+                res["left"] = None
+            except rmlx_kv.RmlxError as e:
+                res["left"] = e.status
+            res["left_s"] = time.monotonic() - t0
+        res["timeout_code"] = _lib.RMLX_E_TIMEOUT
+        res["exhausted_code"] = _lib.RMLX_E_EXHAUSTED
+        out.put((rank, res))
+    except Exception as e:
+        out.put((rank, {"error": repr(e)}))
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def test_two_rank_plan_handshake_failures():
+    """The migration-plan handshake fails on the host, on both ranks where
+    both are present, with nothing allocated: a receiver that cannot hold
+    the blocks (RMLX_E_EXHAUSTED on both), a peer that never answers
+    (RMLX_E_TIMEOUT at the deadline) and a peer that left between steps
+    (RMLX_E_TIMEOUT at once).  No GPU and no NCCL are involved."""
+    ctx = mp.get_context("spawn")
+    out = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_handshake_worker, args=(r, 2, port, out)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(out.get(timeout=240) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    for r in (0, 1):
+        assert "error" not in res[r], res[r]
+    a, b = res[0], res[1]
+    assert a["exhausted"] == b["exhausted"] == a["exhausted_code"]
+    assert a["untouched"] and b["untouched"]
+    assert a["silent"] == a["timeout_code"] and 1.0 <= a["silent_s"] < 10.0
+    assert a["left"] == a["timeout_code"] and a["left_s"] < 5.0
