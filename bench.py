@@ -159,11 +159,15 @@ def prefix_requests(seed, n_req=512, n_prefix=8, prefix_len=1024, suffix=(64, 51
     return np.concatenate(reqs).astype(np.uint32), cu
 
 
-def prefix_pool_size(toks, cu, cub, hashes, block=16):
-    """60% of the distinct blocks the requests need (a dry run with room for all)."""
-    import rmlx_kv
-    m, p = rmlx_kv.PagedCacheManager(block, int(cub[-1])), rmlx_kv.PrefixCacheManager(int(cub[-1]))
-    _, _, st = rmlx_kv.prefix_admit(m, p, toks, cu, hashes, cub)
+def prefix_pool_size(toks, cu, cub, hashes, block=16, impl=None):
+    """60% of the distinct blocks the requests need (a dry run with room for
+    all).  `impl`: the module whose block manager, prefix cache and
+    admission run it (the product's by default; the reference arm passes the
+    oracle)."""
+    if impl is None:
+        import rmlx_kv as impl
+    m, p = impl.PagedCacheManager(block, int(cub[-1])), impl.PrefixCacheManager(int(cub[-1]))
+    st = impl.prefix_admit(m, p, toks, cu, hashes, cub)[2]
     return int(np.ceil(0.6 * st["new_blocks"]))
 
 
@@ -253,6 +257,38 @@ def prefix_cpu(toks, cu, cub, pool):
     orc.prefix_admit(m, p, toks, cu, hashes, cub)
     sec = time.perf_counter() - t0
     return 0.0, sec
+
+
+def run_prefix_reference(args, world):
+    """--impl reference for the prefix workload: the oracle's chain hash and
+    admission of all 512 requests per step, single thread (as the
+    reference), W warm-up and K timed steps; the pool size comes from the
+    oracle's own dry run.  The product library is not loaded."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as orc
+    toks, cu = prefix_requests(0x5EED + 4)
+    cub = np.zeros(len(cu), dtype=np.int64)
+    cub[1:] = np.cumsum((np.diff(cu) + 15) // 16)
+    hashes, _ = orc.hash_chains(toks, cu, np.zeros(len(cu) - 1, dtype=np.uint64), 16)
+    pool = prefix_pool_size(toks, cu, cub, hashes, impl=orc)
+    secs = []
+    for i in range(args.warmup + args.steps):
+        _, sec = prefix_cpu(toks, cu, cub, pool)
+        if i >= args.warmup:
+            secs.append(sec)
+    sec = float(np.median(secs))
+    v = round((len(cu) - 1) / sec, 2)
+    print(json.dumps({"impl": "reference", "metric": PREFIX_METRIC, "value": v, "unit": "admissions/s",
+                      "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                      "ms_per_step": round(sec * 1e3, 2), "higher_is_better": True, "scaling": "replicas",
+                      "vs_baseline": None, "dtype": "u32", "data": "synthetic",
+                      "config": {"workload": PREFIX_DESC, "requests": len(cu) - 1, "tokens": int(len(toks)),
+                                 "blocks": int(cub[-1]), "pool_blocks": pool},
+                      "cpu_baseline": {"value": v, "unit": "admissions/s", "cores": 1, "kind": "port",
+                                       "sample": "oracle chain hash + admission of all 512 requests per step, "
+                                                 "single thread"},
+                      "e2e": {"value": v, "unit": "admissions/s", "h2d_bytes_per_step": 0,
+                              "d2h_bytes_per_step": 0}}), flush=True)
 
 
 L70_METRIC = "KV fork/COW + append + gather HBM GB/s (Llama-3-70B KV shape, KV heads sharded over GPUs)"
@@ -498,10 +534,28 @@ def profile_traffic(name, algorithmic_bytes):
     return round(vals["traffic_bytes_per_launch"] / vals["traffic_algorithmic_bytes"] * algorithmic_bytes)
 
 
-def make_workload(w, steps_total):
-    """Seeded lengths, block tables (through the product's block manager) and
-    per-step slot mappings for `steps_total` steps."""
-    import rmlx_kv
+def _allocate_n(mgr, n):
+    if hasattr(mgr, "allocate_n"):
+        return np.asarray(mgr.allocate_n(n))
+    return np.array([mgr.allocate() for _ in range(n)], dtype=np.int64)
+
+
+def _free_n(mgr, ids):
+    if hasattr(mgr, "free_n"):
+        return mgr.free_n(ids)
+    for b in ids:
+        mgr.free(int(b))
+
+
+def make_workload(w, steps_total, manager=None):
+    """Seeded lengths, block tables and per-step slot mappings for
+    `steps_total` steps.  `manager(block_size, num_blocks)` makes the block
+    manager that hands out the blocks: the product's by default; the
+    reference arm passes the oracle's, which gives the same tables (FIFO
+    reuse of the same permuted free list)."""
+    if manager is None:
+        import rmlx_kv
+        manager = rmlx_kv.PagedCacheManager
     rng = np.random.default_rng(w.seed)
     if w.lens:
         lens0 = np.array(w.lens, dtype=np.int64)
@@ -509,42 +563,44 @@ def make_workload(w, steps_total):
         lens0 = rng.integers(w.ctx_lo, w.ctx_hi + 1, size=w.batch).astype(np.int64)
     need = (lens0 + steps_total + w.block - 1) // w.block
     num_blocks = max(int(np.ceil(1.25 * need.sum())), w.min_blocks)
-    mgr = rmlx_kv.PagedCacheManager(w.block, num_blocks)
+    mgr = manager(w.block, num_blocks)
     # Make the free list a seeded permutation of the pool: allocate all, free
     # in permuted order (FIFO reuse hands them out in that order).
-    mgr.free_n(rng.permutation(mgr.allocate_n(num_blocks)))
+    _free_n(mgr, rng.permutation(_allocate_n(mgr, num_blocks)))
     bt = np.zeros((w.batch, int(need.max())), dtype=np.int32)
     nblk = np.zeros(w.batch, dtype=np.int64)
     for s in range(w.batch):
         n0 = (int(lens0[s]) + w.block - 1) // w.block
-        bt[s, :n0] = mgr.allocate_n(n0)
+        bt[s, :n0] = _allocate_n(mgr, n0)
         nblk[s] = n0
     slots = np.zeros((steps_total, w.batch), dtype=np.int32)
     for st in range(steps_total):
         for s in range(w.batch):
             p = int(lens0[s]) + st
             while p // w.block >= nblk[s]:
-                bt[s, nblk[s]] = mgr.allocate_n(1)[0]
+                bt[s, nblk[s]] = _allocate_n(mgr, 1)[0]
                 nblk[s] += 1
             slots[st, s] = bt[s, p // w.block] * w.block + p % w.block
     return dict(lens0=lens0, bt=bt, slots=slots, num_blocks=num_blocks, mgr=mgr)
 
 
-def step_bytes(w, lens, heads, layers=None):
+def step_bytes(w, lens, heads, layers=None, batch=None):
     """Algorithmic bytes of one step.  Append: read every new row, write its
     stored form (and its scale/zero).  Gather of one layer: read every stored
     row (and meta) of every sequence, write it out in the input type; plus
-    the block-table entries and lengths the gather reads.  K and V both."""
+    the block-table entries and lengths the gather reads.  K and V both.
+    `batch`: sequences appended (default: the workload's batch)."""
     layers = w.layers if layers is None else layers
+    batch = w.batch if batch is None else batch
     i, s, m = w.in_row(heads), w.stored_row(heads), w.meta_row(heads)
-    append = 2 * w.batch * layers * (i + s + m)
+    append = 2 * batch * layers * (i + s + m)
     blocks = int(((lens + w.block - 1) // w.block).sum())
     if w.attn_g:
         # attention reads every stored row once (no gathered copy written),
         # plus the queries it reads and the outputs it writes
-        qo = 2 * w.batch * w.attn_g * i
-        return append, 2 * int(lens.sum()) * (s + m) + 4 * blocks + 4 * w.batch + qo
-    gather_one = 2 * int(lens.sum()) * (s + m + i) + 4 * blocks + 4 * w.batch
+        qo = 2 * batch * w.attn_g * i
+        return append, 2 * int(lens.sum()) * (s + m) + 4 * blocks + 4 * batch + qo
+    gather_one = 2 * int(lens.sum()) * (s + m + i) + 4 * blocks + 4 * batch
     return append, gather_one
 
 
@@ -609,14 +665,16 @@ class Clocks:
                 "samples": len(sm)}
 
 
-def cpu_sample(w, steps, warm, threads, lens0, bt, slots, num_blocks):
+def cpu_sample(w, steps, warm, threads, lens0, bt, slots, num_blocks, seqs=None):
     """The oracle (CPU restatement of the reference) on the host cores: one
     layer of every step -- append 1 token per sequence (quantising it for the
     quantised workloads), then the full gather (dequantise) of that layer,
-    sequences split over `threads`.  Returns (GB/s, seconds per sample)."""
+    sequences split over `threads`.  `seqs`: only the first `seqs` sequences
+    (a bounded sample for slow legs).  Returns (GB/s, seconds per sample)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as orc
     H, D = w.heads, w.head_dim
+    nseq = w.batch if seqs is None else min(seqs, w.batch)
     g = orc.Geo(1, H, D, w.block, num_blocks, 2, bits=w.bits, group_size=w.group,
                 meta_bytes=2 if w.meta == F16 else 4)
     rng = np.random.default_rng(w.seed + 1)
@@ -629,14 +687,15 @@ def cpu_sample(w, steps, warm, threads, lens0, bt, slots, num_blocks):
         meta = np.tile(np.array([0.02, -2.5], dtype=np.float16 if w.meta == F16 else np.float32),
                        (tiles.shape[0], w.block * (D // w.group)))
         tiles[:, w.block * rb:w.block * rb + w.block * mrb] = meta.view(np.uint8)
-    tot = int((lens0 + slots.shape[0]).sum()) * H * D
+    bt = np.ascontiguousarray(bt[:nseq])
+    tot = int((lens0[:nseq] + slots.shape[0]).sum()) * H * D
     ok = np.empty(tot, dtype=np.uint16)
     ov = np.empty(tot, dtype=np.uint16)
-    kin = orc.f32_to_dtype(rng.standard_normal((w.batch, H, D), dtype=np.float32), orc.BF16)
+    kin = orc.f32_to_dtype(rng.standard_normal((nseq, H, D), dtype=np.float32), orc.BF16)
     total_bytes, t_total = 0, 0.0
     for st in range(warm + steps):
-        lens = (lens0 + st + 1).astype(np.int32)
-        sl = slots[st].astype(np.int64)
+        lens = (lens0[:nseq] + st + 1).astype(np.int32)
+        sl = slots[st, :nseq].astype(np.int64)
         t0 = time.perf_counter()
         if w.bits:
             orc.paged_append_quant(pool, g, 0, 1, kin, kin, orc.BF16, 0, H * D, D, sl)
@@ -646,34 +705,58 @@ def cpu_sample(w, steps, warm, threads, lens0, bt, slots, num_blocks):
             orc.paged_gather(pool, g, 0, bt, bt.shape[1], lens, ok, ov, threads=threads)
         dt = time.perf_counter() - t0
         if st >= warm:
-            a, gth = step_bytes(w, lens.astype(np.int64), H, layers=1)
+            a, gth = step_bytes(w, lens.astype(np.int64), H, layers=1, batch=nseq)
             total_bytes += a + gth
             t_total += dt
     return total_bytes / t_total / 1e9, t_total / steps
 
 
+def single_thread_leg(w, steps_available):
+    """Sequences and steps of the single-thread oracle leg: the reference is
+    single-threaded (`&mut self` throughout paged_cache.rs), so this is the
+    reference-faithful CPU figure; bounded to about 10-20 s of work (one
+    step of the workload's steps is its warm-up)."""
+    seqs, steps = (max(1, w.batch // 16), 3) if w.bits else (w.batch, 10)
+    return seqs, max(1, min(steps, steps_available - 1))
+
+
 def run_reference(args, w, rank, world):
-    """--impl reference: the reference's CPU path (the oracle port; the Rust
-    reference cannot be built in this image) on all host cores."""
+    """--impl reference: the reference's CPU path on the host cores.  The
+    Rust reference cannot be built in this image, so this is the oracle
+    (its C++ restatement, oracle/): block tables from the oracle's block
+    manager, the oracle's row-copy append and gather.  The product library
+    is not loaded.  The driver's --steps/--warmup are honoured, each step a
+    sample of one of the layers at the full batch; the pool is sized from
+    the same warm-up + timed steps as the product's arm, so the config is
+    the same."""
     if rank != 0:
         return
     if w.attn_g:
         print(json.dumps({"impl": "reference", "unavailable": "the reference has no attention of its own on this "
                           "path (it runs inside the external rmlx-nn Metal layer cache)"}))
         return
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as orc
     threads = os.cpu_count() or 1
-    steps, warm = max(args.steps // 5, 2), min(args.warmup, 2)
-    wl = make_workload(w, warm + steps)
-    gbs, sec = cpu_sample(w, steps, warm, threads, wl["lens0"], wl["bt"], wl["slots"], wl["num_blocks"])
-    sample = (f"1 of {w.layers} layers per step (append 1 token/seq + full gather of that layer), batch {w.batch}, "
-              f"{steps} timed steps after {warm} warm-up; GB/s is per sampled byte, ms_per_step scaled x{w.layers}")
+    K, W = args.steps, args.warmup
+    wl = make_workload(w, W + K, manager=orc.PagedCacheManager)
+    gbs, sec = cpu_sample(w, K, W, threads, wl["lens0"], wl["bt"], wl["slots"], wl["num_blocks"])
+    s1, k1 = single_thread_leg(w, W + K)
+    gbs1, _ = cpu_sample(w, k1, 1, 1, wl["lens0"], wl["bt"], wl["slots"], wl["num_blocks"], seqs=s1)
+    sample = (f"oracle append + gather, 1 of {w.layers} layers per step at the full batch {w.batch}, "
+              f"{K} timed steps after {W} warm-up, {threads} threads (sequences split over them); GB/s is per "
+              f"sampled byte, ms_per_step the sampled layer's time x{w.layers}")
     print(json.dumps({
         "impl": "reference", "metric": w.metric, "value": round(gbs, 2), "unit": "GB/s", "n_gpus": world,
-        "steps": steps, "warmup": warm, "ms_per_step": round(sec * w.layers * 1e3, 3), "higher_is_better": True,
+        "steps": K, "warmup": W, "ms_per_step": round(sec * w.layers * 1e3, 3), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f16" if w.dtype == F16 else "bf16", "data": "synthetic",
-        "config": config_of(w, w.heads, wl["num_blocks"], 1),
+        "config": config_of(w, w.heads // world, wl["num_blocks"], world),
         "cpu_baseline": {"value": round(gbs, 2), "unit": "GB/s", "cores": threads, "kind": "port",
                          "sample": sample},
+        "single_thread": {"value": round(gbs1, 2), "unit": "GB/s", "cores": 1, "kind": "port",
+                          "sample": f"the reference-faithful figure (the reference is single-threaded): oracle "
+                                    f"append + gather, 1 layer per step, first {s1} of {w.batch} sequences, "
+                                    f"{k1} timed steps after 1 warm-up, 1 thread"},
         "e2e": {"value": round(gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
@@ -714,23 +797,7 @@ def main():
     if args.workload == "prefix":
         if args.impl == "reference":
             if rank == 0:
-                toks, cu = prefix_requests(0x5EED + 4)
-                cub = np.zeros(len(cu), dtype=np.int64)
-                cub[1:] = np.cumsum((np.diff(cu) + 15) // 16)
-                sys.path.insert(0, os.path.join(ROOT, "oracle"))
-                import oracle as orc
-                hashes, _ = orc.hash_chains(toks, cu, np.zeros(len(cu) - 1, dtype=np.uint64), 16)
-                pool = prefix_pool_size(toks, cu, cub, hashes)
-                _, sec = prefix_cpu(toks, cu, cub, pool)
-                v = round((len(cu) - 1) / sec, 2)
-                print(json.dumps({"impl": "reference", "metric": PREFIX_METRIC, "value": v, "unit": "admissions/s",
-                                  "n_gpus": world, "steps": 1, "warmup": 0, "ms_per_step": round(sec * 1e3, 2),
-                                  "higher_is_better": True, "scaling": "replicas", "vs_baseline": None,
-                                  "dtype": "u32", "data": "synthetic", "config": {"workload": PREFIX_DESC},
-                                  "cpu_baseline": {"value": v, "unit": "admissions/s", "cores": 1, "kind": "port",
-                                                   "sample": "all 512 requests, single thread"},
-                                  "e2e": {"value": v, "unit": "admissions/s", "h2d_bytes_per_step": 0,
-                                          "d2h_bytes_per_step": 0}}), flush=True)
+                run_prefix_reference(args, world)
             return
         return run_prefix(args, rank, world)
     if args.workload == "llama70b":
@@ -1068,10 +1135,16 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and not G:
         threads = os.cpu_count() or 1
-        steps = 8 if not w.bits else 3
+        steps = min(8 if not w.bits else 3, W + K - 1)
         gbs, _ = cpu_sample(w, steps, 1, threads, lens0, bt, slots, num_blocks)
+        s1, k1 = single_thread_leg(w, W + K)
+        gbs1, _ = cpu_sample(w, k1, 1, 1, lens0, bt, slots, num_blocks, seqs=s1)
         cpu = {"value": round(gbs, 2), "unit": "GB/s", "cores": threads, "kind": "port",
-               "sample": f"oracle append+gather, 1 of {L} layers per step, batch {B}, {steps} timed steps"}
+               "sample": f"oracle append+gather, 1 of {L} layers per step, batch {B}, {steps} timed steps, "
+                         f"sequences split over {threads} threads",
+               "single_thread": {"value": round(gbs1, 2), "unit": "GB/s", "cores": 1,
+                                 "sample": f"reference-faithful (the reference is single-threaded): 1 layer per "
+                                           f"step, first {s1} of {B} sequences, {k1} timed steps, 1 thread"}}
 
     if rank == 0:
         print(json.dumps({
