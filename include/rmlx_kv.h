@@ -355,7 +355,9 @@ RMLX_API rmlx_status rmlx_kv_gather(rmlx_kv_pool* p, int32_t layer, const int32_
  * more is flagged in the pool's device error word (rmlx_kv_pool_check bit 4)
  * and leaves out unwritten.  Launches on one pool hand out work through a
  * counter the pool owns: order them on one stream (or otherwise one after
- * another), not concurrently. */
+ * another), not concurrently.  The counter is made with the pool
+ * (rmlx_kv_pool_new), so no attention call allocates device memory or
+ * synchronises the device. */
 RMLX_API rmlx_status rmlx_kv_attention_workspace_size(const rmlx_kv_pool* p, int32_t q_heads_per_kv, int32_t num_seqs,
                                                       int64_t max_total_tokens, size_t* bytes);
 RMLX_API rmlx_status rmlx_kv_decode_attention(rmlx_kv_pool* p, int32_t layer, const void* q, int32_t q_heads_per_kv,

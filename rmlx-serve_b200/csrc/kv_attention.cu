@@ -1770,14 +1770,8 @@ rmlx_status rmlx_kv_decode_attention(rmlx_kv_pool* p, int32_t layer, const void*
                                   : (bf ? attn_combine_cta_kernel<RMLX_BF16, 64> : attn_combine_cta_kernel<RMLX_F16, 64>))
                      : (hd == 128 ? (bf ? attn_combine_kernel<RMLX_BF16, 128> : attn_combine_kernel<RMLX_F16, 128>)
                                   : (bf ? attn_combine_kernel<RMLX_BF16, 64> : attn_combine_kernel<RMLX_F16, 64>));
-  if (!p->attn_work) {  // the item counter: pool memory, zero between launches
-    void* w = nullptr;
-    if (cudaMalloc(&w, 16) != cudaSuccess || cudaMemset(w, 0, 16) != cudaSuccess) {
-      if (w) cudaFree(w);
-      return cuda_check(cudaGetLastError(), "attention item counter");
-    }
-    p->attn_work = static_cast<unsigned long long*>(w);
-  }
+  // p->attn_work, the item counter, is pool memory made by rmlx_kv_pool_new
+  // and zero between launches: this call allocates nothing.
   rmlx_status s;
   if (p->attn_nseq != num_seqs || p->attn_G != G) {  // the launch shape, kept for the next call with the same shape
     const AttnPlan plan = attn_plan(p, num_seqs, G);

@@ -775,16 +775,29 @@ rmlx_status rmlx_kv_pool_new(const rmlx_pool_config* cfg, int device, rmlx_kv_po
     cudaFree(p.base);
     return s;
   }
-  if ((s = cuda_check(cudaMemset(p.base, 0, p.bytes), "cudaMemset(pool)")) != RMLX_OK ||
-      (s = cuda_check(cudaMemset(p.err, 0, sizeof(int32_t)), "cudaMemset(err)")) != RMLX_OK) {
+  // The decode attention's work-item counter lives with the pool, so that no
+  // attention call allocates (a first call may then sit inside a stream
+  // capture); the kernels leave it at zero between launches.
+  void* work = nullptr;
+  if ((s = cuda_check(cudaMalloc(&work, 16), "cudaMalloc(attention counter)")) != RMLX_OK) {
     cudaFree(p.base);
     cudaFree(p.err);
+    return s;
+  }
+  p.attn_work = static_cast<unsigned long long*>(work);
+  if ((s = cuda_check(cudaMemset(p.base, 0, p.bytes), "cudaMemset(pool)")) != RMLX_OK ||
+      (s = cuda_check(cudaMemset(p.err, 0, sizeof(int32_t)), "cudaMemset(err)")) != RMLX_OK ||
+      (s = cuda_check(cudaMemset(p.attn_work, 0, 16), "cudaMemset(attention counter)")) != RMLX_OK) {
+    cudaFree(p.base);
+    cudaFree(p.err);
+    cudaFree(p.attn_work);
     return s;
   }
   *out = new (std::nothrow) rmlx_kv_pool(p);
   if (!*out) {
     cudaFree(p.base);
     cudaFree(p.err);
+    cudaFree(p.attn_work);
     return fail(RMLX_E_EXHAUSTED, "host allocation failed");
   }
   return RMLX_OK;
@@ -796,7 +809,7 @@ void rmlx_kv_pool_destroy(rmlx_kv_pool* p) {
     DeviceGuard dg(p->device);
     cudaFree(p->base);
     cudaFree(p->err);
-    if (p->attn_work) cudaFree(p->attn_work);
+    cudaFree(p->attn_work);
   }
   delete p;
 }

@@ -353,6 +353,7 @@ rmlx_status rmlx_qcache_raw(rmlx_qcache* q, size_t layer, int32_t which, uint8_t
                             float* zr, size_t gcap, size_t* n_bytes, size_t* n_groups) {
   if (!q || !n_bytes || !n_groups) return fail(RMLX_E_BAD_ARG, "NULL argument");
   if (layer >= q->layers) return fail(RMLX_E_RANGE, "layer %zu out of range", layer);
+  if (which != 0 && which != 1) return fail(RMLX_E_BAD_ARG, "which must be 0 (keys) or 1 (values)");
   QLayer& L = which ? q->v[layer] : q->k[layer];
   *n_bytes = L.bytes.len;
   *n_groups = L.scales.len;
