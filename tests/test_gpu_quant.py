@@ -4,9 +4,10 @@ Codes, scales and zeros must be bit-identical to the oracle's restatement of
 quantize_group (quantized_cache.rs:232-273); dequantised rows must be
 bit-identical to dequantize_group's f32 `code * scale + zero`
 (quantized_cache.rs:278-296) rounded to the output type, i.e. within 0.5 ulp
-of the reference's f32 value.  With f16 metadata the codes are still exact
-and the dequantised value is checked against the f32-metadata value with a
-stated bound.
+of the reference's f32 value.  With f16 metadata the codes are still exact,
+the dequantised rows are bit-identical to the oracle's `code * scale16 +
+zero16`, and their distance from the f32-metadata value is measured in f16
+ulps of the group's magnitude against a stated bound.
 """
 import numpy as np
 import pytest
@@ -97,29 +98,33 @@ def test_constant_groups_use_unit_scale(cuda):
     assert (out.cpu().numpy() == 42.0).all()
 
 
-def test_f16_meta_error_bound(cuda):
-    """fp16 scale/zero: codes identical to f32 metadata, dequant differs from
-    the reference's f32 value by at most the metadata rounding."""
+@pytest.mark.parametrize("bits", [8, 4])
+def test_f16_meta_ulp_vs_f32_reference(cuda, bits):
+    """fp16 scale/zero on the GPU: bit-exact to the oracle with either
+    metadata, and within the stated bound (f16 ulps of the group's largest
+    |value|) of the reference's f32 `code * scale + zero`, with the figure
+    test_f16_meta_ulp.py reports for the same rows."""
     import torch
-    rng = np.random.default_rng(14)
-    L, H, D, bs, N, T = 1, 8, 128, 16, 8, 64
-    k = rand_rows(rng, (L, T, H, D), orc.BF16, 0.01)
-    slots = np.arange(T, dtype=np.int32)
-    outs = {}
+    from test_f16_meta_ulp import BOUND, MEASURED, dequant_both, rows, ulp_error
+    T, H, D, bs = 8192, 8, 128, 16
+    N = T // bs
+    x = rows(T, H, D, 0x5EED + 3)
+    want32, want16 = dequant_both(bits, T, H, D)
+    got = {}
     for meta in (orc.F32, orc.F16):
-        pool = rmlx_kv.KVPool(L, H, D, bs, N, dtype=orc.BF16, quant_bits=8, group_size=64,
-                              meta_dtype=meta)
-        pool.append(to_dev(k), to_dev(k), to_dev(slots), T)
-        bt = np.arange(4, dtype=np.int32).reshape(1, 4)
-        o = torch.empty(T * H * D, dtype=torch.int16, device=cuda)
-        pool.gather(0, to_dev(bt), 4, to_dev(np.array([T], np.int32)), 1, o, torch.empty_like(o))
-        outs[meta] = orc.dtype_to_f32(to_host(o, np.uint16), orc.BF16)
+        pool = rmlx_kv.KVPool(1, H, D, bs, N, dtype=orc.F32, quant_bits=bits, group_size=64, meta_dtype=meta)
+        pool.append(to_dev(x), to_dev(x), to_dev(np.arange(T, dtype=np.int32)), T)
+        o = torch.empty(T * H * D, dtype=torch.float32, device=cuda)
+        pool.gather(0, to_dev(np.arange(N, dtype=np.int32).reshape(1, N)), N, to_dev(np.array([T], np.int32)), 1,
+                    o, torch.empty_like(o))
+        torch.cuda.synchronize()
+        assert pool.check() == 0
+        got[meta] = o.cpu().numpy()
         pool.close()
-    x = orc.dtype_to_f32(k, orc.BF16).reshape(T, H, D).transpose(1, 0, 2).reshape(-1)
-    err32 = np.abs(outs[orc.F32] - x).max()
-    err16 = np.abs(outs[orc.F16] - x).max()
-    # 8-bit: |error| <= scale/2 + bf16 rounding; scale <= (range)/255 with range ~ <= 2*8*4.5
-    assert err32 < 0.25 and err16 < 0.3
+    np.testing.assert_array_equal(got[orc.F32], want32)
+    np.testing.assert_array_equal(got[orc.F16], want16)
+    e = ulp_error(got[orc.F32], got[orc.F16])
+    assert e <= BOUND and e == MEASURED[bits]
 
 
 # (head_dim, block_size, out dtype, group): every dequant kernel path.
