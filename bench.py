@@ -750,7 +750,8 @@ def run_reference(args, w, rank, world):
         "impl": "reference", "metric": w.metric, "value": round(gbs, 2), "unit": "GB/s", "n_gpus": world,
         "steps": K, "warmup": W, "ms_per_step": round(sec * w.layers * 1e3, 3), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f16" if w.dtype == F16 else "bf16", "data": "synthetic",
-        "config": config_of(w, w.heads // world, wl["num_blocks"], world),
+        "config": config_of(w, w.heads // world, wl["num_blocks"], world,
+                            not w.attn_g and not w.bits and args.gather == "layers"),
         "cpu_baseline": {"value": round(gbs, 2), "unit": "GB/s", "cores": threads, "kind": "port",
                          "sample": sample},
         "single_thread": {"value": round(gbs1, 2), "unit": "GB/s", "cores": 1, "kind": "port",
@@ -761,7 +762,7 @@ def run_reference(args, w, rank, world):
     }), flush=True)
 
 
-def config_of(w, H, num_blocks, world):
+def config_of(w, H, num_blocks, world, multi=None):
     c = {"workload": w.desc, "batch": w.batch, "layers": w.layers, "kv_heads": w.heads, "kv_heads_per_gpu": H,
          "head_dim": w.head_dim, "block_size": w.block, "pool_blocks": num_blocks, "sharding": f"kv-head x{world}",
          "l2": ("inputs larger than L2: each gather launch moves >0.1 GB, no flush" if not w.lens else
@@ -769,6 +770,9 @@ def config_of(w, H, num_blocks, world):
     if w.bits:
         c.update({"quant_bits": w.bits, "group_size": w.group, "meta": "f16" if w.meta == F16 else "f32",
                   "outliers": w.outliers})
+    if multi is not None and not w.attn_g:
+        c["gather"] = ("one rmlx_kv_gather_layers launch per step for all layers, each layer into its own output"
+                       if multi else "one rmlx_kv_gather launch per layer, into a reused per-layer output")
     if w.graph:
         c["launch"] = ("device-timed steps replayed from one CUDA graph of the K steps' library launches; "
                        "the e2e loop runs the planner and stages each step's inputs on the host, then replays "
@@ -791,6 +795,8 @@ def main():
     ap.add_argument("--layers", type=int, default=None,
                     help="layers in the pool (profiling runs only; a gather moves the same bytes per layer)")
     ap.add_argument("--quick", action="store_true", help="device-timed loop only (profiling runs)")
+    ap.add_argument("--gather", default="layers", choices=["layers", "per-layer"],
+                    help="plain pools: one multi-layer gather launch per step, or one launch per layer")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank, world = env_int("RANK", 0), env_int("WORLD_SIZE", 1)
@@ -881,6 +887,9 @@ def main():
     lens_steps = np.stack([(lens0 + s + 1).astype(np.int32) for s in range(W + K)])
     lens_d = torch.from_numpy(lens_steps).cuda()
     G = w.attn_g
+    # one rmlx_kv_gather_layers launch per step for all layers, each into its
+    # own output, instead of one rmlx_kv_gather per layer into a reused buffer
+    multi = not G and not w.bits and args.gather == "layers"
     if G:
         # per-layer queries of the step, attention output, split workspace
         q_d = rand_rows((L, B, H * G, D))
@@ -890,8 +899,9 @@ def main():
         scale = 1.0 / float(np.sqrt(D))
         out_k = out_v = None
     else:
-        out_k = torch.empty(int(lens_steps[-1].sum()) * H * D, device="cuda", dtype=tdt)
+        out_k = torch.empty(int(lens_steps[-1].sum()) * H * D * (L if multi else 1), device="cuda", dtype=tdt)
         out_v = torch.empty_like(out_k)
+    layer_elems = int(lens_steps[-1].sum()) * H * D  # each layer's gathered K (or V), elements
     ls = B * H * D
 
     def launch_step(s, ev_pair=None, sp=sp, gathers_only=False):
@@ -905,7 +915,10 @@ def main():
                                     slots_d[s].data_ptr(), B, sp)
         if ev_pair is not None:
             ev_pair[0].record(stream)
-        for layer in range(L):
+        if multi:
+            rc |= lib.rmlx_kv_gather_layers(h, 0, L, bt_d.data_ptr(), bt.shape[1], lens_d[s].data_ptr(), B,
+                                            out_k.data_ptr(), out_v.data_ptr(), layer_elems, sp)
+        for layer in range(0 if multi else L):
             if G:
                 rc |= lib.rmlx_kv_decode_attention(h, layer, q_d[layer].data_ptr(), G, bt_d.data_ptr(), bt.shape[1],
                                                    lens_d[s].data_ptr(), B, scale, att_out.data_ptr(),
@@ -970,10 +983,10 @@ def main():
         g_gathers.replay()
         ev[0][1].record(stream)
         torch.cuda.synchronize()
-        gather_ms = [ev[0][0].elapsed_time(ev[0][1]) / (K * L)]
+        gather_ms = [ev[0][0].elapsed_time(ev[0][1]) / (K * (1 if multi else L))]
     else:
-        # average gather launch = a step's gather span / its L launches
-        gather_ms = [ev[i][0].elapsed_time(ev[i][1]) / L for i in range(K)]
+        # average gather launch = a step's gather span / its launches
+        gather_ms = [ev[i][0].elapsed_time(ev[i][1]) / (1 if multi else L) for i in range(K)]
     if rc or pool.check() != 0:
         raise SystemExit("launch or device-side validation error in the timed region")
 
@@ -982,7 +995,7 @@ def main():
     for i in range(K):
         a, g1 = step_bytes(w, lens_steps[W + i].astype(np.int64), H)
         tot_bytes += a + L * g1
-        gather_bytes += [g1] * L
+        gather_bytes += [L * g1] if multi else [g1] * L
     tot_bytes *= world
     value = tot_bytes / (elapsed_ms * 1e-3) / 1e9
     ms_per_step = elapsed_ms / K
@@ -1070,7 +1083,10 @@ def main():
             torch.cuda.current_stream().wait_event(copied[b])
         rc |= lib.rmlx_kv_append(h, 0, L, dk[b].data_ptr(), dv[b].data_ptr(), ls, ts, hs, d_slots[b].data_ptr(), B,
                                  sp_b)
-        for layer in range(L):
+        if multi:
+            rc |= lib.rmlx_kv_gather_layers(h, 0, L, d_bt[b].data_ptr(), bt.shape[1], d_lens[b].data_ptr(), B,
+                                            out_k.data_ptr(), out_v.data_ptr(), layer_elems, sp_b)
+        for layer in range(0 if multi else L):
             if G:
                 rc |= lib.rmlx_kv_decode_attention(h, layer, dq[b][layer].data_ptr(), G, d_bt[b].data_ptr(),
                                                    bt.shape[1], d_lens[b].data_ptr(), B, scale, att_out.data_ptr(),
@@ -1152,14 +1168,14 @@ def main():
             "warmup": W, "ms_per_step": round(ms_per_step, 4), "us_per_step": round(ms_per_step * 1e3, 1),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "f16" if w.dtype == F16 else "bf16",
-            "data": "synthetic", "config": config_of(w, H, num_blocks, world),
+            "data": "synthetic", "config": config_of(w, H, num_blocks, world, multi),
             "roofline": {"bound": "hbm", "kernel": w.kernel, "achieved": round(achieved, 1), "peak": peak,
                          "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "frac_of_8000_nominal": round(achieved / 8000.0, 4), "traffic": traffic,
                          "algorithmic_bytes_per_launch": int(g_bytes), "launch_ms": round(g_ms, 4)},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": 4, "ms_per_step": round(e2e_s / K * 1e3, 4)},
-            "gpu_launches": K * (1 + (2 if G else 1) * L),
+            "gpu_launches": K * (1 + (1 if multi else (2 if G else 1) * L)),
             "cpu_baseline": cpu,
             "clocks": clk,
         }), flush=True)

@@ -337,6 +337,19 @@ RMLX_API rmlx_status rmlx_kv_append(rmlx_kv_pool* p, int32_t layer_begin, int32_
 RMLX_API rmlx_status rmlx_kv_gather(rmlx_kv_pool* p, int32_t layer, const int32_t* block_tables, int32_t block_table_stride,
                            const int32_t* seq_lens, int32_t num_seqs, void* out_k, void* out_v, void* stream);
 
+/* Gather of layers [layer_begin, layer_begin + num_layers) in one launch:
+ * the same rows as num_layers calls of rmlx_kv_gather, layer layer_begin + i
+ * written at out_k / out_v + i * out_layer_stride (elements of cfg.dtype; a
+ * multiple of 16 bytes).  The counterpart of rmlx_kv_append's layer range
+ * (both replace per-layer get_logical_order calls, rotating_cache.rs:162-197,
+ * over a whole step).  One launch walks each pool block's tiles of every
+ * layer in pool order and scans seq_lens once; quantised pools are
+ * dequantised one launch per layer. */
+RMLX_API rmlx_status rmlx_kv_gather_layers(rmlx_kv_pool* p, int32_t layer_begin, int32_t num_layers,
+                                           const int32_t* block_tables, int32_t block_table_stride,
+                                           const int32_t* seq_lens, int32_t num_seqs, void* out_k, void* out_v,
+                                           int64_t out_layer_stride, void* stream);
+
 /* Paged decode attention: the consumer of the K/V tiles, reading them in
  * place (no counterpart in the reference crate, whose attention runs inside
  * the external rmlx-nn layer cache, kv_cache.rs:30,50; listed as the next

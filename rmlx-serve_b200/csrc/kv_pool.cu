@@ -77,16 +77,25 @@ struct TileRef {
   int n16;
 };
 
-__device__ __forceinline__ TileRef gather_tile(const PoolGeo& g, int layer, int64_t u, int64_t units,
+__device__ __forceinline__ TileRef gather_tile(const PoolGeo& g, int layer0, int nl, int64_t u, int64_t units,
                                                const int32_t* __restrict__ bt, int bt_stride, const int32_t* cub,
                                                const int32_t* cut, int nseq, uint8_t* ok, uint8_t* ov,
-                                               int64_t out_row_bytes, int lane, int32_t* err) {
+                                               int64_t out_row_bytes, int64_t out_layer_bytes, int lane,
+                                               int32_t* err) {
   TileRef t{nullptr, nullptr, 0};
   if (u >= units) return t;
+  // unit u = (gathered block gi, layer l, kv, head h), head fastest: the
+  // units of one block are its tiles in pool order
   const int h = (int)(u % g.heads);
-  const int64_t q = u / g.heads;
+  int64_t q = u / g.heads;
   const int kv = (int)(q & 1);
-  const int64_t gi = q >> 1;
+  q >>= 1;
+  int dl = 0;
+  if (nl > 1) {
+    dl = (int)(q % nl);
+    q /= nl;
+  }
+  const int64_t gi = q;
   const int s = find_seq(cub, nseq, gi);
   const int b = (int)(gi - cub[s]);
   const int L = cut[s + 1] - cut[s];
@@ -95,28 +104,34 @@ __device__ __forceinline__ TileRef gather_tile(const PoolGeo& g, int layer, int6
     if (lane == 0) atomicOr(err, DEV_ERR_BLOCK);
     return t;
   }
-  t.src = g.base + g.tile_off(blk, layer, kv, h);
-  t.dst = (kv ? ov : ok) + ((int64_t)cut[s] * g.heads + (int64_t)h * L + (int64_t)b * g.bs) * out_row_bytes;
+  t.src = g.base + g.tile_off(blk, layer0 + dl, kv, h);
+  t.dst = (kv ? ov : ok) + dl * out_layer_bytes +
+          ((int64_t)cut[s] * g.heads + (int64_t)h * L + (int64_t)b * g.bs) * out_row_bytes;
   t.n16 = min(g.bs, L - b * g.bs) * g.row_bytes / 16;
   return t;
 }
 
-__global__ void __launch_bounds__(256, 2) gather_rows_kernel(PoolGeo g, int layer, const int32_t* __restrict__ bt,
-                                                             int bt_stride, const int32_t* __restrict__ lens,
-                                                             int nseq, uint8_t* __restrict__ ok,
-                                                             uint8_t* __restrict__ ov, int32_t* err) {
+// nl layers from layer0 in one launch (rmlx_kv_gather: nl = 1); layer
+// layer0 + i lands at out + i * out_layer_bytes.
+__global__ void __launch_bounds__(256, 2) gather_rows_kernel(PoolGeo g, int layer0, int nl,
+                                                             const int32_t* __restrict__ bt, int bt_stride,
+                                                             const int32_t* __restrict__ lens, int nseq,
+                                                             uint8_t* __restrict__ ok, uint8_t* __restrict__ ov,
+                                                             int64_t out_layer_bytes, int32_t* err) {
   extern __shared__ int32_t smem[];
   int32_t* cub = smem;
   int32_t* cut = smem + nseq + 1;
   pdl_wait();
   pdl_release();
   scan_seq_lens(lens, nseq, g.bs, cub, cut);
-  const int64_t units = (int64_t)cub[nseq] * 2 * g.heads;
+  const int64_t units = (int64_t)cub[nseq] * nl * 2 * g.heads;
   const int lane = threadIdx.x & 31;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   for (int64_t u = ((blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5) * 2; u < units; u += nwarps * 2) {
-    const TileRef a = gather_tile(g, layer, u, units, bt, bt_stride, cub, cut, nseq, ok, ov, g.row_bytes, lane, err);
-    const TileRef b = gather_tile(g, layer, u + 1, units, bt, bt_stride, cub, cut, nseq, ok, ov, g.row_bytes, lane, err);
+    const TileRef a = gather_tile(g, layer0, nl, u, units, bt, bt_stride, cub, cut, nseq, ok, ov, g.row_bytes,
+                                  out_layer_bytes, lane, err);
+    const TileRef b = gather_tile(g, layer0, nl, u + 1, units, bt, bt_stride, cub, cut, nseq, ok, ov, g.row_bytes,
+                                  out_layer_bytes, lane, err);
     warp_copy2(a.src, a.dst, a.n16, b.src, b.dst, b.n16, lane);
   }
 }
@@ -898,17 +913,22 @@ rmlx_status rmlx_kv_append(rmlx_kv_pool* p, int32_t layer_begin, int32_t num_lay
   return cuda_check(cudaGetLastError(), "append launch");
 }
 
-rmlx_status rmlx_kv_gather(rmlx_kv_pool* p, int32_t layer, const int32_t* bt, int32_t bt_stride, const int32_t* lens,
-                           int32_t nseq, void* out_k, void* out_v, void* stream) {
+static rmlx_status gather_impl(rmlx_kv_pool* p, int32_t layer, int32_t nl, const int32_t* bt, int32_t bt_stride,
+                               const int32_t* lens, int32_t nseq, void* out_k, void* out_v, int64_t out_layer_stride,
+                               void* stream) {
   if (!p) return fail(RMLX_E_BAD_ARG, "NULL pool");
   const rmlx_pool_config& c = p->cfg;
-  if (layer < 0 || layer >= c.num_layers) return fail(RMLX_E_RANGE, "layer %d outside the pool's %d layers", layer, c.num_layers);
+  if (layer < 0 || nl < 0 || layer + nl > c.num_layers)
+    return fail(RMLX_E_RANGE, "layers [%d, %d) outside the pool's %d layers", layer, layer + nl, c.num_layers);
   if (nseq < 0 || nseq > RMLX_MAX_SEQS_PER_LAUNCH)
     return fail(RMLX_E_BAD_ARG, "num_seqs %d outside [0, %d]", nseq, RMLX_MAX_SEQS_PER_LAUNCH);
-  if (nseq == 0) return RMLX_OK;
+  if (nseq == 0 || nl == 0) return RMLX_OK;
   if (!bt || !lens || !out_k || !out_v) return fail(RMLX_E_BAD_ARG, "NULL block_tables, seq_lens or outputs");
   if (bt_stride < 0) return fail(RMLX_E_BAD_ARG, "block_table_stride < 0");
   if (!aligned16(out_k) || !aligned16(out_v)) return fail(RMLX_E_BAD_ARG, "outputs must be 16-byte aligned");
+  const int64_t out_layer_bytes = out_layer_stride * dtype_size(c.dtype);
+  if (nl > 1 && (out_layer_stride <= 0 || out_layer_bytes % 16))
+    return fail(RMLX_E_BAD_ARG, "out_layer_stride must be positive and a multiple of 16 bytes");
   DeviceGuard dg(p->device);
   cudaStream_t st = (cudaStream_t)stream;
   PoolGeo g = p->geo();
@@ -921,8 +941,9 @@ rmlx_status rmlx_kv_gather(rmlx_kv_pool* p, int32_t layer, const int32_t* bt, in
       p->gather_grid = persistent_grid(gather_rows_kernel, 256, smem, p->num_sms);
       p->gather_smem = smem;
     }
-    cudaError_t e = launch_pdl(gather_rows_kernel, dim3(p->gather_grid), dim3(256), smem, st, g, layer, bt, bt_stride,
-                               lens, nseq, (uint8_t*)out_k, (uint8_t*)out_v, p->err);
+    cudaError_t e = launch_pdl(gather_rows_kernel, dim3(p->gather_grid), dim3(256), smem, st, g, layer, nl, bt,
+                               bt_stride, lens, nseq, (uint8_t*)out_k, (uint8_t*)out_v, nl > 1 ? out_layer_bytes : 0,
+                               p->err);
     if (e != cudaSuccess) return cuda_check(e, "gather launch");
   } else {
     const int ept = c.dtype == RMLX_F32 ? 4 : 8;  // output elements per 16-byte task
@@ -936,12 +957,28 @@ rmlx_status rmlx_kv_gather(rmlx_kv_pool* p, int32_t layer, const int32_t* bt, in
       p->gather_grid = persistent_grid(fn, 256, smem, p->num_sms);
       p->gather_smem = smem;
     }
-    cudaError_t e = launch_pdl(fn, dim3(p->gather_grid), dim3(256), smem, st, g, layer, bt, bt_stride, lens, nseq,
-                               (uint8_t*)out_k, (uint8_t*)out_v, (int)c.head_dim, log2i(c.group_size),
-                               is_pow2(tpr) ? log2i(tpr) : -1, p->err);
-    if (e != cudaSuccess) return cuda_check(e, "gather launch");
+    // one launch per layer (the dequantising kernels take one layer)
+    for (int32_t i = 0; i < nl; ++i) {
+      cudaError_t e = launch_pdl(fn, dim3(p->gather_grid), dim3(256), smem, st, g, layer + i, bt, bt_stride, lens,
+                                 nseq, (uint8_t*)out_k + i * out_layer_bytes, (uint8_t*)out_v + i * out_layer_bytes,
+                                 (int)c.head_dim, log2i(c.group_size), is_pow2(tpr) ? log2i(tpr) : -1, p->err);
+      if (e != cudaSuccess) return cuda_check(e, "gather launch");
+    }
   }
   return cuda_check(cudaGetLastError(), "gather launch");
+}
+
+rmlx_status rmlx_kv_gather(rmlx_kv_pool* p, int32_t layer, const int32_t* bt, int32_t bt_stride, const int32_t* lens,
+                           int32_t nseq, void* out_k, void* out_v, void* stream) {
+  if (p && (layer < 0 || layer >= p->cfg.num_layers))
+    return fail(RMLX_E_RANGE, "layer %d outside the pool's %d layers", layer, p->cfg.num_layers);
+  return gather_impl(p, layer, 1, bt, bt_stride, lens, nseq, out_k, out_v, 0, stream);
+}
+
+rmlx_status rmlx_kv_gather_layers(rmlx_kv_pool* p, int32_t layer_begin, int32_t num_layers, const int32_t* bt,
+                                  int32_t bt_stride, const int32_t* lens, int32_t nseq, void* out_k, void* out_v,
+                                  int64_t out_layer_stride, void* stream) {
+  return gather_impl(p, layer_begin, num_layers, bt, bt_stride, lens, nseq, out_k, out_v, out_layer_stride, stream);
 }
 
 static rmlx_status launch_copy(rmlx_kv_pool* p, const int32_t* a, const int32_t* b, int32_t n, int mode,

@@ -155,6 +155,7 @@ _sig("rmlx_kv_pool_write", st, vp, C.c_size_t, C.c_size_t, vp)
 _sig("rmlx_kv_append", st, vp, C.c_int32, C.c_int32, vp, vp, C.c_int64, C.c_int64, C.c_int64, vp,
      C.c_int32, vp)
 _sig("rmlx_kv_gather", st, vp, C.c_int32, vp, C.c_int32, vp, C.c_int32, vp, vp, vp)
+_sig("rmlx_kv_gather_layers", st, vp, C.c_int32, C.c_int32, vp, C.c_int32, vp, C.c_int32, vp, vp, C.c_int64, vp)
 _sig("rmlx_kv_attention_workspace_size", st, vp, C.c_int32, C.c_int32, C.c_int64, C.POINTER(C.c_size_t))
 _sig("rmlx_kv_decode_attention", st, vp, C.c_int32, vp, C.c_int32, vp, C.c_int32, vp, C.c_int32, C.c_float, vp, vp,
      C.c_size_t, vp)

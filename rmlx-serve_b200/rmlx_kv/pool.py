@@ -120,6 +120,14 @@ class KVPool:
         check(lib.rmlx_kv_gather(self._h, layer, _ptr(block_tables), block_table_stride, _ptr(seq_lens),
                                  num_seqs, _ptr(out_k), _ptr(out_v), _stream(stream, self.device)))
 
+    def gather_layers(self, layer_begin: int, num_layers: int, block_tables, block_table_stride: int, seq_lens,
+                      num_seqs: int, out_k, out_v, out_layer_stride: int, stream=None) -> None:
+        """Layers [layer_begin, layer_begin + num_layers) in one launch; layer
+        layer_begin + i at element offset i * out_layer_stride of out_k/out_v."""
+        check(lib.rmlx_kv_gather_layers(self._h, layer_begin, num_layers, _ptr(block_tables), block_table_stride,
+                                        _ptr(seq_lens), num_seqs, _ptr(out_k), _ptr(out_v), out_layer_stride,
+                                        _stream(stream, self.device)))
+
     def attention_workspace_size(self, q_heads_per_kv: int, num_seqs: int, max_total_tokens: int) -> int:
         n = C.c_size_t()
         check(lib.rmlx_kv_attention_workspace_size(self._h, q_heads_per_kv, num_seqs, max_total_tokens, C.byref(n)))

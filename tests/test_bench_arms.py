@@ -51,7 +51,7 @@ def test_reference_arm_is_oracle_only_and_honours_steps():
     assert rec["value"] > 0 and rec["single_thread"]["cores"] == 1
     import bench
     w = bench.WORKLOADS["config1"]
-    assert rec["config"] == bench.config_of(w, w.heads, bench.make_workload(w, 7)["num_blocks"], 1)
+    assert rec["config"] == bench.config_of(w, w.heads, bench.make_workload(w, 7)["num_blocks"], 1, True)
 
 
 def test_prefix_reference_arm_is_oracle_only():

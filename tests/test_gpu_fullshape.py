@@ -8,6 +8,7 @@ compares with the oracle on the same inputs:
 
 * the decode step at the Llama-3.1-8B KV shape (batch 64, ctx U[512,4096],
   bf16): pool bytes after the append and the gathered K/V, byte for byte;
+  and the multi-layer gather (rmlx_kv_gather_layers) at that shape;
 * the quantised store (batch 128, ctx U[1024,8192], 8- and 4-bit codes,
   group 64, fp16 scale/zero, N(0,1) with 1% outliers x8): the prompts are
   quantised on append on both sides, then one decode step; codes, scales,
@@ -73,7 +74,9 @@ def _rand_rows(gen, shape, outliers):
 
 
 def _host16(t):
-    return np.ascontiguousarray(t.cpu().numpy().view(np.uint16))
+    """A 16-bit device tensor's bits on the host (uint16)."""
+    import torch
+    return np.ascontiguousarray(t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16))
 
 
 def _append_both(pool, host, g, k, v, slots, T, quant):
@@ -160,6 +163,38 @@ def test_decode_step_llama8b_layer(cuda):
     _same(pool.read(), host, "pool after the append")
     _same(gk, ek, "gathered K")
     _same(gv, ev, "gathered V")
+    pool.close()
+
+
+def test_gather_layers_llama8b(cuda):
+    """rmlx_kv_gather_layers at the decode shape (batch 64, ctx U[512,4096],
+    8 KV heads x 128, bf16) over 4 layers in one launch, each layer's output
+    at its own offset, against the oracle's per-layer gathers."""
+    import torch
+    w = bench.WORKLOADS["decode"]
+    wl = bench.make_workload(w, 1)
+    L, H, D, BS, B, N = 4, w.heads, w.head_dim, w.block, w.batch, wl["num_blocks"]
+    pool = rmlx_kv.KVPool(L, H, D, BS, N, dtype=rmlx_kv.BF16)
+    gen = torch.Generator(device="cuda").manual_seed(w.seed + 1)
+    _view(pool, torch.bfloat16).normal_(generator=gen)
+    torch.cuda.synchronize()
+    host = pool.read()
+    g = orc.Geo(L, H, D, BS, N, 2)
+    lens = (wl["lens0"] + 1).astype(np.int32)
+    bt = wl["bt"]
+    tot = int(lens.sum()) * H * D
+    ok = torch.empty(L * tot, dtype=torch.int16, device="cuda")
+    ov = torch.empty_like(ok)
+    btd, lnd = to_dev(bt), to_dev(lens)
+    _lib.check(_lib.lib.rmlx_kv_gather_layers(pool.handle, 0, L, btd.data_ptr(), bt.shape[1], lnd.data_ptr(), B,
+                                              ok.data_ptr(), ov.data_ptr(), tot, _sp()))
+    torch.cuda.synchronize()
+    assert pool.check() == 0
+    for layer in range(L):
+        ek, ev = np.empty(tot, np.uint16), np.empty(tot, np.uint16)
+        assert orc.paged_gather(host, g, layer, bt, bt.shape[1], lens, ek, ev, threads=THREADS) == 0
+        _same(ok[layer * tot:(layer + 1) * tot].cpu().numpy().view(np.uint16), ek, f"layer {layer} K")
+        _same(ov[layer * tot:(layer + 1) * tot].cpu().numpy().view(np.uint16), ev, f"layer {layer} V")
     pool.close()
 
 

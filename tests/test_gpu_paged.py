@@ -189,3 +189,79 @@ def test_bad_arguments_rejected(cuda):
         pool.append(d, d, d, 1, layer_begin=1, num_layers=2)
     with pytest.raises(rmlx_kv.RmlxError):
         pool.gather(0, d, 1, d, 8193, d, d)  # too many sequences for one launch
+
+
+def _gather_layers_case(cuda, L, H, D, bs, N, dt, lens, l0, nl, seed, bits=0, gs=64, meta=orc.F16):
+    """rmlx_kv_gather_layers over layers [l0, l0 + nl) equals the oracle's
+    per-layer gathers, each at its layer offset, with padding between the
+    layers' outputs left untouched."""
+    import torch
+    rng = np.random.default_rng(seed)
+    lens = np.array(lens, dtype=np.int64)
+    bt, _ = block_tables(rng, lens, bs, N)
+    qkw = dict(quant_bits=bits, group_size=gs, meta_dtype=meta) if bits else {}
+    pool = rmlx_kv.KVPool(L, H, D, bs, N, dtype=dt, **qkw)
+    g = orc.Geo(L, H, D, bs, N, ESIZE[dt], bits=bits, group_size=gs, meta_bytes=4 if meta == orc.F32 else 2)
+    if bits:
+        host = np.zeros(g.pool_bytes(), dtype=np.uint8)
+        pos = [(s, p) for s in range(len(lens)) for p in range(lens[s])]
+        k = rand_rows(rng, (L, len(pos), H, D), dt, 0.01)
+        v = rand_rows(rng, (L, len(pos), H, D), dt, 0.01)
+        slots = slots_for(bt, bs, pos)
+        assert orc.paged_append_quant(host, g, 0, L, k, v, dt, len(pos) * H * D, H * D, D, slots) == 0
+        pool.append(to_dev(k), to_dev(v), to_dev(slots), len(pos))
+    else:
+        host = rng.integers(0, 256, size=g.pool_bytes(), dtype=np.uint8)
+        pool.write(host)
+    final = lens.astype(np.int32)
+    tot = int(final.sum()) * H * D
+    npdt = NP_DT[dt]
+    stride = tot + 24  # elements between layers: 16-byte multiple, with a gap
+    ok = torch.full((nl * stride * ESIZE[dt],), 0x5A, dtype=torch.uint8, device=cuda)
+    ov = torch.full_like(ok, 0x5A)
+    pool.gather_layers(l0, nl, to_dev(bt), bt.shape[1], to_dev(final), len(final), ok, ov, stride)
+    torch.cuda.synchronize()
+    assert pool.check() == 0
+    gk, gv = to_host(ok, npdt).reshape(nl, stride), to_host(ov, npdt).reshape(nl, stride)
+    pad = np.full(24 * ESIZE[dt], 0x5A, dtype=np.uint8).view(npdt)
+    for i in range(nl):
+        ek, ev = np.zeros(tot, dtype=npdt), np.zeros(tot, dtype=npdt)
+        if bits:
+            assert orc.paged_gather_dequant(host, g, l0 + i, bt, bt.shape[1], final, ek, ev, dt) == 0
+        else:
+            assert orc.paged_gather(host, g, l0 + i, bt, bt.shape[1], final, ek, ev) == 0
+        np.testing.assert_array_equal(gk[i, :tot], ek)
+        np.testing.assert_array_equal(gv[i, :tot], ev)
+        np.testing.assert_array_equal(gk[i, tot:], pad)
+    pool.close()
+
+
+@pytest.mark.parametrize("l0,nl", [(0, 4), (1, 2), (3, 1)])
+def test_gather_layers(cuda, l0, nl):
+    _gather_layers_case(cuda, 4, 3, 128, 16, 96, orc.BF16, [1, 15, 16, 17, 0, 300, 33], l0, nl, seed=20 + l0 + nl)
+
+
+@pytest.mark.parametrize("dt,D,bs", [(orc.F32, 64, 8), (orc.F16, 256, 32), (orc.BF16, 64, 1)])
+def test_gather_layers_dtypes(cuda, dt, D, bs):
+    _gather_layers_case(cuda, 3, 2, D, bs, 400 // bs + 40, dt, [5, 0, 40, 129], 0, 3, seed=25)
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+def test_gather_layers_quantised(cuda, bits):
+    """Quantised pools: one dequantising launch per layer, same offsets."""
+    _gather_layers_case(cuda, 3, 2, 128, 16, 64, orc.BF16, [3, 64, 100], 0, 3, seed=27, bits=bits)
+
+
+def test_gather_layers_bad_arguments(cuda):
+    import torch
+    pool = rmlx_kv.KVPool(4, 1, 64, 16, 4, dtype=orc.BF16)
+    d = torch.zeros(256, dtype=torch.int32, device=cuda)
+    with pytest.raises(rmlx_kv.RmlxError):
+        pool.gather_layers(2, 3, d, 1, d, 1, d, d, 64)  # past the last layer
+    with pytest.raises(rmlx_kv.RmlxError):
+        pool.gather_layers(0, 2, d, 1, d, 1, d, d, 4)  # 8-byte layer stride
+    with pytest.raises(rmlx_kv.RmlxError):
+        pool.gather_layers(0, 2, d, 1, d, 1, d, d, 0)
+    pool.gather_layers(0, 0, d, 1, d, 1, d, d, 64)  # no layers: a no-op
+    assert pool.check() == 0
+    pool.close()
