@@ -299,12 +299,15 @@ L70_DESC = ("Llama-3-70B KV: 80 layers x 8 KV heads x 128, block 16, bf16; batch
 
 
 def l70_plan(seed, steps, batch=256, block=16, fork_frac=0.05):
-    """Host plan of the fork/append steps, identical on every rank: per step
-    a few sequences are replaced by forks of others, then each sequence
-    appends one token (copy-on-write of a shared tail).  Returns per step
-    the copy pairs, slots, block table and lengths after the append."""
+    """Host plan of the fork/append steps, identical on every rank, made by
+    the library's batch planner (rmlx_kv_batch_*): per step a few sequences
+    are replaced by forks of others (remove, then fork into the freed row),
+    then each sequence appends one token (copy-on-write of a shared tail).
+    Returns per step the copy pairs, slots, block table and lengths after
+    the append; the pool size; the block manager and the planner (which
+    holds the sequences' block references while it lives)."""
     import rmlx_kv
-    from rmlx_kv.batch import SequenceBlocks
+    from rmlx_kv.batch import KVBatch
     rng = np.random.default_rng(seed)
     lens = np.exp(rng.uniform(np.log(2048), np.log(32768), size=batch)).astype(np.int64)
     nfork = max(1, int(round(fork_frac * batch)))
@@ -313,16 +316,26 @@ def l70_plan(seed, steps, batch=256, block=16, fork_frac=0.05):
     num_blocks = int(((lens + block - 1) // block).sum()) + (steps + 1) * (batch + nfork)
     mgr = rmlx_kv.PagedCacheManager(block, num_blocks)
     mgr.free_n(rng.permutation(mgr.allocate_n(num_blocks)))  # scatter the free list
-    seqs = SequenceBlocks(mgr, block, lens)
+    planner = KVBatch(mgr, None, batch)
+    uids = np.arange(1, batch + 1, dtype=np.uint64)  # uids[row]
+    for r in range(batch):
+        row, _, _ = planner.add(int(uids[r]), rng.integers(0, 128256, size=int(lens[r]), dtype=np.uint32))
+        assert row == r
+    next_uid = batch + 1
     plan = []
     for _ in range(steps):
         idx = rng.permutation(batch)
         for parent, child in zip(idx[:nfork], idx[nfork:2 * nfork]):
-            seqs.fork(int(parent), int(child))
-        cow_src, cow_dst, slots = seqs.append_slots()
-        plan.append(dict(cow_src=cow_src, cow_dst=cow_dst, slots=slots, bt=seqs.block_table(),
-                         lens=seqs.seq_lens()))
-    return plan, num_blocks, mgr
+            planner.remove(int(uids[child]))
+            row = planner.fork(int(uids[parent]), next_uid)
+            assert row == child
+            uids[child] = next_uid
+            next_uid += 1
+        slots, cow_src, cow_dst = planner.step(uids, rng.integers(0, 128256, size=batch, dtype=np.uint32))
+        bt, ln = planner.tables()
+        plan.append(dict(cow_src=cow_src.copy(), cow_dst=cow_dst.copy(), slots=slots.copy(), bt=bt.copy(),
+                         lens=ln.copy()))
+    return plan, num_blocks, mgr, planner
 
 
 def run_llama70b(args, rank, world):
@@ -344,7 +357,7 @@ def run_llama70b(args, rank, world):
     w = Workload("llama70b", L70_METRIC, L70_DESC, 0x5EED + 5, layers=LAYERS_FULL, batch=B, bits=args.bits)
     off, H = rd.shard_heads(HEADS, world, rank)
     W, K = args.warmup, args.steps
-    plan, num_blocks, mgr = l70_plan(w.seed, W + K)
+    plan, num_blocks, mgr, planner = l70_plan(w.seed, W + K)
     qkw = dict(quant_bits=w.bits, group_size=w.group, meta_dtype=w.meta) if w.bits else {}
     probe = rmlx_kv.KVPool(1, H, D, BS, 1, dtype=rmlx_kv.BF16, head_offset=off, device=dev, **qkw)
     tile = probe.layout.tile_bytes

@@ -460,8 +460,9 @@ RMLX_API rmlx_status rmlx_prompt_cache_load(rmlx_kv_pool* p, const char* path, c
  * RotatingKVCache (rotating_cache.rs:16-283) on paged blocks: a sequence of
  * max_size ring positions keeps its first `keep` and cycles the rest; ring
  * position p is block table entry p / block_size, row p % block_size.  The
- * host holds the reference's (written, offset) state (rmlx_kv.batch.
- * RotatingBlocks) and appends through slot mappings.
+ * reference's (written, offset) state lives in an rmlx_rotating (below),
+ * which hands out the slot mappings, ring offsets and trim moves for these
+ * device calls.
  * rmlx_kv_gather_ring: get_logical_order (:162-197) of layer `layer` for
  * num_seqs sequences: output as rmlx_kv_gather, seq_lens[s] rows; logical
  * row i reads ring position i when ring_offsets[s] < 0 (nothing rotated, the
@@ -477,6 +478,46 @@ RMLX_API rmlx_status rmlx_kv_gather_ring(rmlx_kv_pool* p, int32_t layer, const i
                                          void* out_k, void* out_v, void* stream);
 RMLX_API rmlx_status rmlx_kv_move_rows(rmlx_kv_pool* p, const int32_t* src_slots, const int32_t* dst_slots, int32_t n,
                                        void* stream);
+
+/* RotatingKVCache's host state (rotating_cache.rs:16-283) for one sequence,
+ * over a PagedCacheManager whose blocks hold the ring (destroy the ring
+ * before the manager).  The state advances once per token for all of a
+ * pool's layers (the reference advances it per per-layer append call: the
+ * same for a one-layer cache, or per layer driven as its own cache).
+ *   new (:45-83): keep >= max_size -> RMLX_E_BAD_ARG (the reference
+ *     panics); block_size must be the manager's.
+ *   destroy / release: the ring's blocks go back to the manager (release
+ *     keeps the object, empty).
+ *   append_slots (:94-143): slots[0..n) of n new tokens, in order, for
+ *     rmlx_kv_append; blocks are taken from the manager as the ring first
+ *     reaches them, all before any state changes (RMLX_E_EXHAUSTED leaves
+ *     the ring unchanged).  A position written twice within one call keeps
+ *     the later token; the earlier token's slot is -1 (skipped).
+ *   seq_len (:201-203), can_trim (:253-255), written, max_size, keep.
+ *   ring_offset: the ring_offsets entry of rmlx_kv_gather_ring: -1 while
+ *     written <= max_size, else the reference's offset.
+ *   trim (:213-247): n > trimmable -> RMLX_E_RANGE (the reference panics),
+ *     state unchanged.  Before the ring rotates, the rows above the trimmed
+ *     ones shift down: *n_moves (src, dst) slot pairs for rmlx_kv_move_rows
+ *     (at most max_size; RMLX_E_BAD_ARG and no change when cap is short);
+ *     after it rotates only the offset moves (*n_moves = 0).
+ *   blocks: the ring's block ids in ring order (its block-table row);
+ *     *n_blocks always, the ids when out holds them. */
+typedef struct rmlx_rotating rmlx_rotating;
+RMLX_API rmlx_status rmlx_rotating_new(rmlx_block_manager* m, int32_t block_size, int32_t max_size, int32_t keep,
+                                       rmlx_rotating** out);
+RMLX_API void rmlx_rotating_destroy(rmlx_rotating* r);
+RMLX_API void rmlx_rotating_release(rmlx_rotating* r);
+RMLX_API rmlx_status rmlx_rotating_append_slots(rmlx_rotating* r, int32_t n, int32_t* slots);
+RMLX_API size_t rmlx_rotating_seq_len(const rmlx_rotating* r);
+RMLX_API int32_t rmlx_rotating_can_trim(const rmlx_rotating* r);
+RMLX_API int32_t rmlx_rotating_ring_offset(const rmlx_rotating* r);
+RMLX_API size_t rmlx_rotating_written(const rmlx_rotating* r);
+RMLX_API size_t rmlx_rotating_max_size(const rmlx_rotating* r);
+RMLX_API size_t rmlx_rotating_keep(const rmlx_rotating* r);
+RMLX_API rmlx_status rmlx_rotating_trim(rmlx_rotating* r, int32_t n, int32_t* src_slots, int32_t* dst_slots,
+                                        int32_t cap, int32_t* n_moves);
+RMLX_API rmlx_status rmlx_rotating_blocks(const rmlx_rotating* r, int32_t* out, int32_t cap, int32_t* n_blocks);
 
 /* Block copy for copy-on-write / fork: every tile of block src[i] is copied
  * to block dst[i] (all layers, K and V, all heads of the pool).  src/dst are

@@ -161,6 +161,18 @@ _sig("rmlx_kv_decode_attention", st, vp, C.c_int32, vp, C.c_int32, vp, C.c_int32
      C.c_size_t, vp)
 _sig("rmlx_kv_copy_blocks", st, vp, vp, vp, C.c_int32, vp)
 
+# RotatingKVCache state over a block manager
+_sig("rmlx_rotating_new", st, vp, C.c_int32, C.c_int32, C.c_int32, C.POINTER(vp))
+_sig("rmlx_rotating_destroy", None, vp)
+_sig("rmlx_rotating_release", None, vp)
+_sig("rmlx_rotating_append_slots", st, vp, C.c_int32, i32p)
+for _n in ("seq_len", "written", "max_size", "keep"):
+    _sig(f"rmlx_rotating_{_n}", C.c_size_t, vp)
+_sig("rmlx_rotating_can_trim", C.c_int32, vp)
+_sig("rmlx_rotating_ring_offset", C.c_int32, vp)
+_sig("rmlx_rotating_trim", st, vp, C.c_int32, i32p, i32p, C.c_int32, i32p)
+_sig("rmlx_rotating_blocks", st, vp, i32p, C.c_int32, i32p)
+
 
 class BatchStats(C.Structure):
     _fields_ = [(n, C.c_uint64) for n in ("admitted", "rejected", "prompt_tokens", "cached_tokens", "new_blocks",

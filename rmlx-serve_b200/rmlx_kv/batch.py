@@ -111,88 +111,96 @@ class SequenceBlocks:
 class RotatingBlocks:
     """One sliding-window sequence as a ring over its blocks: the
     (written, offset) state machine of RotatingKVCache (rotating_cache.rs:
-    16-283) with ring position p stored in block table entry p / block_size,
-    row p % block_size.  Blocks are taken from the manager as the ring first
-    reaches them (the reference preallocates max_size rows).
+    16-283) kept by the library (rmlx_rotating_* in the C ABI), with ring
+    position p stored in block table entry p / block_size, row
+    p % block_size.  Blocks are taken from the manager (this package's
+    PagedCacheManager) as the ring first reaches them; the reference
+    preallocates max_size rows.
 
     The state advances once per token for all layers of the pool; the
     reference advances it on every per-layer append call, which is the same
     for a one-layer cache (its tests) and for each layer driven as its own
-    cache.
+    cache.  The reference's panics (keep >= max_size, trimming more than is
+    trimmable) raise ValueError here.
     """
 
     def __init__(self, mgr, block_size: int, max_size: int, keep: int):
-        if keep >= max_size:  # rotating_cache.rs:45-48
-            raise ValueError(f"keep ({keep}) must be less than max_size ({max_size})")
-        self.mgr, self.bs = mgr, int(block_size)
-        self.max_size, self.keep = int(max_size), int(keep)
-        self.offset = 0
-        self.written = 0
-        self.table: List[int] = []
+        h = _lib.vp()
+        rc = _lib.lib.rmlx_rotating_new(mgr._h, block_size, max_size, keep, C.byref(h))
+        if rc == _lib.RMLX_E_BAD_ARG:
+            raise ValueError(_lib.lib.rmlx_last_error().decode())
+        _lib.check(rc)
+        self._h, self._mgr = h, mgr
+        self.bs, self.max_size, self.keep = int(block_size), int(max_size), int(keep)
+        mgr._dependents.add(self)
 
-    def _slot(self, pos: int) -> int:
-        while pos // self.bs >= len(self.table):
-            bid = self.mgr.allocate()
-            if bid is None:
-                raise PoolExhausted("no free block")
-            self.table.append(int(bid))
-        return self.table[pos // self.bs] * self.bs + pos % self.bs
+    def __del__(self):
+        self.close()
+
+    def close(self):
+        """Return the ring's blocks to the manager and drop the ring."""
+        if getattr(self, "_h", None):
+            # When a garbage-collected cycle took the manager first, its
+            # blocks are gone with it: only the ring's own memory is left.
+            if getattr(self._mgr, "_h", None):
+                _lib.lib.rmlx_rotating_destroy(self._h)
+            self._h = None
+
+    @property
+    def table(self) -> List[int]:
+        """The ring's blocks, in ring order."""
+        n = C.c_int32()
+        _lib.check(_lib.lib.rmlx_rotating_blocks(self._h, None, 0, C.byref(n)))
+        out = np.zeros(max(n.value, 1), np.int32)
+        _lib.check(_lib.lib.rmlx_rotating_blocks(self._h, out.ctypes.data_as(_lib.i32p), len(out), C.byref(n)))
+        return out[:n.value].tolist()
+
+    @property
+    def written(self) -> int:
+        return int(_lib.lib.rmlx_rotating_written(self._h))
 
     def append_slots(self, n: int) -> np.ndarray:
         """Slots of n new tokens in order (append, :94-143).  A ring position
         written twice within the call keeps the later token: the earlier
-        token's slot is -1 (skipped by rmlx_kv_append)."""
-        rotating = self.max_size - self.keep
-        slots = np.empty(n, dtype=np.int32)
-        last = {}
-        for t in range(n):
-            pos = self.written if self.written < self.max_size else self.keep + self.offset
-            slots[t] = self._slot(pos)
-            if pos in last:
-                slots[last[pos]] = -1
-            last[pos] = t
-            if self.written >= self.max_size:
-                self.offset = (self.offset + 1) % rotating
-            self.written += 1
-        return slots
+        token's slot is -1 (skipped by rmlx_kv_append).  Raises
+        PoolExhausted, with the state unchanged, when the blocks the tokens
+        reach cannot be had."""
+        slots = np.empty(max(n, 1), dtype=np.int32)
+        rc = _lib.lib.rmlx_rotating_append_slots(self._h, n, slots.ctypes.data_as(_lib.i32p))
+        if rc == _lib.RMLX_E_EXHAUSTED:
+            raise PoolExhausted(_lib.lib.rmlx_last_error().decode())
+        _lib.check(rc)
+        return slots[:n]
 
     def seq_len(self) -> int:  # :201-203
-        return min(self.written, self.max_size)
+        return int(_lib.lib.rmlx_rotating_seq_len(self._h))
 
     def can_trim(self) -> bool:  # :253-255
-        return self.seq_len() > self.keep
+        return bool(_lib.lib.rmlx_rotating_can_trim(self._h))
 
     def ring_offset(self) -> int:
         """For rmlx_kv_gather_ring: -1 before the ring has rotated
         (written <= max_size), else the offset of its oldest row."""
-        return -1 if self.written <= self.max_size else self.offset
+        return int(_lib.lib.rmlx_rotating_ring_offset(self._h))
 
     def trim(self, n: int):
         """Drop the n oldest rows after `keep` (trim, :213-247).  Before the
         ring rotates the rows above them shift down: returns the (src, dst)
         slot lists that rmlx_kv_move_rows must apply; after, only the state
         moves (empty lists)."""
-        trimmable = max(self.seq_len() - self.keep, 0)
-        if n > trimmable:
-            raise ValueError(f"cannot trim {n} tokens: only {trimmable} trimmable")
-        src, dst = [], []
-        if self.written <= self.max_size:
-            remaining = self.written - self.keep - n
-            for r in range(remaining):
-                src.append(self._slot(self.keep + n + r))
-                dst.append(self._slot(self.keep + r))
-            self.written -= n
-        else:
-            rotating = self.max_size - self.keep
-            self.offset = (self.offset + n) % rotating
-            self.written -= n
-        return np.array(src, dtype=np.int32), np.array(dst, dtype=np.int32)
+        src = np.empty(max(self.max_size, 1), np.int32)
+        dst = np.empty_like(src)
+        nm = C.c_int32()
+        rc = _lib.lib.rmlx_rotating_trim(self._h, n, src.ctypes.data_as(_lib.i32p), dst.ctypes.data_as(_lib.i32p),
+                                         len(src), C.byref(nm))
+        if rc in (_lib.RMLX_E_RANGE, _lib.RMLX_E_BAD_ARG):
+            raise ValueError(_lib.lib.rmlx_last_error().decode())
+        _lib.check(rc)
+        return src[:nm.value].copy(), dst[:nm.value].copy()
 
     def release(self) -> None:
-        for b in self.table:
-            self.mgr.free(b)
-        self.table = []
-        self.written = self.offset = 0
+        """Return the ring's blocks to the manager; the ring starts empty."""
+        _lib.lib.rmlx_rotating_release(self._h)
 
 
 class KVBatch:
@@ -216,7 +224,13 @@ class KVBatch:
 
     def close(self):
         if getattr(self, "_h", None):
-            _lib.lib.rmlx_kv_batch_destroy(self._h)
+            # When a garbage-collected cycle took the manager or the prefix
+            # cache first (their weak references to this batch were cleared
+            # before it could be closed), the references it held went with
+            # them: destroying the batch would touch freed state.
+            alive = getattr(self._mgr, "_h", None) and (self._prefix is None or getattr(self._prefix, "_h", None))
+            if alive:
+                _lib.lib.rmlx_kv_batch_destroy(self._h)
             self._h = None
 
     def add(self, uid: int, prompt: Sequence[int]):

@@ -232,7 +232,7 @@ def test_fork_step_llama70b_one_head_shard(cuda, bits):
     of shared tails), appends and gathers, as the bench plans them."""
     import torch
     B, D, BS = 256, 128, 16
-    plan, N, _ = bench.l70_plan(0x5EED + 5, 2)
+    plan, N, _, _planner = bench.l70_plan(0x5EED + 5, 2)
     qkw = dict(quant_bits=8, group_size=64, meta_dtype=rmlx_kv.F16) if bits else {}
     pool = rmlx_kv.KVPool(1, 1, D, BS, N, dtype=rmlx_kv.BF16, head_offset=7, **qkw)
     g = orc.Geo(1, 1, D, BS, N, 2, bits=bits, group_size=64, meta_bytes=2)

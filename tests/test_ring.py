@@ -83,3 +83,48 @@ def test_reference_unit_tests():
         RotatingBlocks(m, 2, 5, 5)
     with pytest.raises(ValueError, match="cannot trim"):
         rb2.trim(3)
+
+
+def test_exhausted_pool_leaves_ring_unchanged():
+    """append_slots takes every block the new tokens reach before changing
+    any state: with too few free blocks it fails and the ring is as before."""
+    from rmlx_kv.batch import PoolExhausted
+    m = rmlx_kv.PagedCacheManager(4, 3)
+    rb = RotatingBlocks(m, 4, 16, 2)
+    rb.append_slots(5)  # 2 blocks
+    before = (rb.seq_len(), rb.written, rb.ring_offset(), rb.table, m.num_free_blocks())
+    with pytest.raises(PoolExhausted):
+        rb.append_slots(8)  # reaches position 12: 4 blocks
+    assert (rb.seq_len(), rb.written, rb.ring_offset(), rb.table, m.num_free_blocks()) == before
+    assert len(rb.append_slots(7)) == 7  # up to position 11: the third block
+    assert m.num_free_blocks() == 0
+
+
+def test_trim_reports_moves_and_rejects_short_buffers():
+    import ctypes as C
+    from rmlx_kv import _lib
+    m = rmlx_kv.PagedCacheManager(4, 8)
+    rb = RotatingBlocks(m, 4, 10, 1)
+    rb.append_slots(7)
+    nm = C.c_int32()
+    buf = np.zeros(8, np.int32)
+    p = buf.ctypes.data_as(_lib.i32p)
+    # 7 rows, keep 1, trim 2: rows 3..6 move to 1..4; a 3-entry buffer is short
+    assert _lib.lib.rmlx_rotating_trim(rb._h, 2, p, p, 3, C.byref(nm)) == _lib.RMLX_E_BAD_ARG
+    assert nm.value == 4 and rb.seq_len() == 7
+    src, dst = rb.trim(2)
+    assert len(src) == 4 and rb.seq_len() == 5
+    t = rb.table
+    assert list(src) == [t[p // 4] * 4 + p % 4 for p in range(3, 7)]
+    assert list(dst) == [t[p // 4] * 4 + p % 4 for p in range(1, 5)]
+
+
+def test_ring_closes_before_its_manager():
+    m = rmlx_kv.PagedCacheManager(2, 8)
+    rb = RotatingBlocks(m, 2, 6, 0)
+    rb.append_slots(6)
+    assert m.num_free_blocks() == 5
+    del m  # the ring still holds the manager; closing the ring frees its blocks
+    mgr = rb._mgr
+    rb.close()
+    assert mgr.num_free_blocks() == 8
