@@ -415,6 +415,13 @@ RMLX_API rmlx_status rmlx_kv_batch_tables(const rmlx_kv_batch* b, int32_t* block
 RMLX_API rmlx_status rmlx_kv_batch_seq(const rmlx_kv_batch* b, uint64_t uid, int32_t* row, int32_t* len,
                                        int32_t* block_ids, int32_t cap, int32_t* nblocks);
 RMLX_API void rmlx_kv_batch_stats(const rmlx_kv_batch* b, rmlx_batch_stats* out);
+/* BatchKVCache::active_count (batch_cache.rs:68-70): live sequences. */
+RMLX_API int32_t rmlx_kv_batch_num_active(const rmlx_kv_batch* b);
+/* BatchKVCache::iter (batch_cache.rs:100-106): for rows [0, min(cap,
+ * *num_rows)), uids[row] (0 for a free row) and live[row]; either may be
+ * NULL.  *num_rows = max_seqs. */
+RMLX_API rmlx_status rmlx_kv_batch_rows(const rmlx_kv_batch* b, uint64_t* uids, int32_t* live, int32_t cap,
+                                        int32_t* num_rows);
 
 /* ---- Prompt cache files (prompt_cache.rs:63-210) --------------------------
  * A sequence's K/V as a safetensors file: one [seq_len, head_dim] tensor per

@@ -327,4 +327,18 @@ void rmlx_kv_batch_stats(const rmlx_kv_batch* b, rmlx_batch_stats* out) {
   if (b && out) *out = b->stats;
 }
 
+int32_t rmlx_kv_batch_num_active(const rmlx_kv_batch* b) {
+  return b ? (int32_t)b->by_uid.size() : 0;
+}
+
+rmlx_status rmlx_kv_batch_rows(const rmlx_kv_batch* b, uint64_t* uids, int32_t* live, int32_t cap, int32_t* num_rows) {
+  if (!b || !num_rows) return fail(RMLX_E_BAD_ARG, "NULL batch or num_rows");
+  *num_rows = (int32_t)b->rows.size();
+  for (int32_t r = 0; r < cap && r < *num_rows; ++r) {
+    if (uids) uids[r] = b->rows[r].live ? b->rows[r].uid : 0;
+    if (live) live[r] = b->rows[r].live ? 1 : 0;
+  }
+  return RMLX_OK;
+}
+
 }  // extern "C"

@@ -189,6 +189,8 @@ _sig("rmlx_kv_batch_step", st, vp, u64p, u32p, C.c_int32, i32p, i32p, i32p, i32p
 _sig("rmlx_kv_batch_tables", st, vp, i32p, C.c_int32, i32p, C.c_int32, i32p, i32p)
 _sig("rmlx_kv_batch_seq", st, vp, C.c_uint64, i32p, i32p, i32p, C.c_int32, i32p)
 _sig("rmlx_kv_batch_stats", None, vp, C.POINTER(BatchStats))
+_sig("rmlx_kv_batch_num_active", C.c_int32, vp)
+_sig("rmlx_kv_batch_rows", st, vp, u64p, i32p, C.c_int32, i32p)
 _sig("rmlx_kv_gather_ring", st, vp, C.c_int32, vp, C.c_int32, vp, vp, C.c_int32, C.c_int32, C.c_int32, vp, vp, vp)
 _sig("rmlx_kv_move_rows", st, vp, vp, vp, C.c_int32, vp)
 cpp = C.POINTER(C.c_char_p)

@@ -287,6 +287,20 @@ class KVBatch:
                                               len(ids), C.byref(nb)))
         return row.value, ln.value, ids[:nb.value]
 
+    def num_active(self) -> int:
+        """Live sequences (BatchKVCache::active_count)."""
+        return int(_lib.lib.rmlx_kv_batch_num_active(self._h))
+
+    def rows(self):
+        """-> uids [max_seqs] uint64 (0 for a free row) and a live mask
+        (BatchKVCache::iter over (row, sequence))."""
+        uids = np.zeros(self.max_seqs, np.uint64)
+        live = np.zeros(self.max_seqs, np.int32)
+        n = C.c_int32()
+        _lib.check(_lib.lib.rmlx_kv_batch_rows(self._h, uids.ctypes.data_as(C.POINTER(C.c_uint64)),
+                                               live.ctypes.data_as(_lib.i32p), self.max_seqs, C.byref(n)))
+        return uids[:n.value], live[:n.value].astype(bool)
+
     def stats(self) -> dict:
         s = _lib.BatchStats()
         _lib.lib.rmlx_kv_batch_stats(self._h, s)

@@ -127,3 +127,37 @@ def test_exhaustion_is_all_or_nothing():
     np.testing.assert_array_equal(before[1], after[1])
     assert m.num_free_blocks() == 1
     b.close()
+
+
+def test_batch_kv_cache_mapping():
+    """The reference's BatchKVCache tests (batch_cache.rs:120-197) through
+    the calls that replace it: insert -> add (the batch picks the lowest
+    free row), get/get_mut -> seq, remove -> remove, active_count ->
+    num_active, iter -> rows, capacity -> max_seqs.  compact has nothing to
+    move: rows are block-table rows, and a free row is a zero-length row."""
+    m = rmlx_kv.PagedCacheManager(4, 64)
+    b = KVBatch(m, None, 4)
+    assert b.max_seqs == 4 and b.num_active() == 0
+    # insert at 0, 1, 2 (lowest free rows), then remove 0: rows 1 and 2 live
+    for uid in (10, 11, 12):
+        row, cached, slots = b.add(uid, [1, 2, 3])
+        assert row == uid - 10 and cached == 0 and len(slots) == 3
+    b.remove(10)
+    assert b.num_active() == 2
+    uids, live = b.rows()
+    assert list(np.flatnonzero(live)) == [1, 2] and list(uids) == [0, 11, 12, 0]
+    with pytest.raises(rmlx_kv.RmlxError):
+        b.seq(10)  # removed: get(0) is None
+    assert b.seq(11)[0] == 1
+    with pytest.raises(rmlx_kv.RmlxError):
+        b.remove(10)  # remove of an empty slot
+    bt, lens = b.tables()
+    assert list(lens) == [0, 3, 3]  # rows up to the last live one; the gap is a zero-length row
+    # the next admission takes the gap
+    assert b.add(13, [4])[0] == 0
+    b.add(14, [5])
+    with pytest.raises(rmlx_kv.RmlxError):
+        b.add(15, [6])  # capacity 4 exceeded
+    assert b.num_active() == 4
+    b.close()
+    assert m.num_free_blocks() == 64
