@@ -396,7 +396,16 @@ RMLX_API rmlx_status rmlx_kv_decode_attention(rmlx_kv_pool* p, int32_t layer, co
  *        the prefix cache first).
  *   tables: rows [0, *num_rows) as block_tables[row][stride] (0-padded) and
  *        seq_lens[row] (0 for a free row); both NULL = size query.
- * The batch holds references in the block manager: destroy it first. */
+ * The batch holds references in the block manager: destroy it first.
+ * BatchKVCache (batch_cache.rs:13-114) maps onto it as: new(capacity) ->
+ * rmlx_kv_batch_new(max_seqs = capacity); insert -> add (the batch picks the
+ * lowest free row and returns it); get / get_mut -> seq; remove -> remove;
+ * active_count -> num_active; iter -> rows; compact -> nothing to move (a
+ * row is a row of the step's block table, a free row a zero-length row that
+ * the kernels skip).  KVCache::new / preallocated (kv_cache.rs:28-54) and
+ * make_prompt_cache (prompt_cache.rs:31-45) have no per-sequence object: one
+ * rmlx_kv_pool_new per GPU holds every sequence's blocks, and add admits a
+ * sequence. */
 typedef struct rmlx_kv_batch rmlx_kv_batch;
 typedef struct {
   uint64_t admitted, rejected, prompt_tokens, cached_tokens, new_blocks, evictions, cow_copies;
