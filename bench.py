@@ -1015,10 +1015,27 @@ def main():
     g_bytes = float(np.mean(gather_bytes))
     g_ms = float(np.mean(gather_ms))
 
+    # The append alone: the K timed steps' appends again, back to back, CUDA
+    # events around them (each launch overlaps the previous one's tail, as
+    # in the step); average launch = span / K.
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record(stream)
+    for i in range(K):
+        rc |= lib.rmlx_kv_append(h, 0, L, new_k[W + i].data_ptr(), new_v[W + i].data_ptr(), ls, ts, hs,
+                                 slots_d[W + i].data_ptr(), B, sp)
+    a1.record(stream)
+    torch.cuda.synchronize()
+    if rc or pool.check() != 0:
+        raise SystemExit("launch or device-side validation error in the append timing")
+    append_ms = a0.elapsed_time(a1) / K
+    append_bytes = step_bytes(w, lens_steps[W].astype(np.int64), H)[0]
+
     if args.quick:
         clocks.stop()
         if rank == 0:
             print(json.dumps({"quick": True, "workload": w.name, "layers": L, "ms_per_step": round(ms_per_step, 4),
+                              "append_ms": round(append_ms, 4),
+                              "append_gbs": round(append_bytes / (append_ms * 1e-3) / 1e9, 1),
                               "value": round(value, 2), "gather_launch_ms": round(g_ms, 4),
                               "gather_gbs": round(g_bytes / (g_ms * 1e-3) / 1e9, 1)}))
         pool.close()
@@ -1186,6 +1203,11 @@ def main():
                          "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "frac_of_8000_nominal": round(achieved / 8000.0, 4), "traffic": traffic,
                          "algorithmic_bytes_per_launch": int(g_bytes), "launch_ms": round(g_ms, 4)},
+            "append": {"kernel": "append_quant_kernel" if w.bits else "append_rows_kernel",
+                       "algorithmic_bytes_per_launch": int(append_bytes), "launch_ms": round(append_ms, 4),
+                       "achieved": round(append_bytes / (append_ms * 1e-3) / 1e9, 1),
+                       "frac": round(append_bytes / (append_ms * 1e-3) / 1e9 / peak, 4),
+                       "what": "the timed steps' appends again, back to back (all layers, one launch per step)"},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": 4, "ms_per_step": round(e2e_s / K * 1e3, 4)},
             "gpu_launches": K * (1 + (1 if multi else (2 if G else 1) * L)),
