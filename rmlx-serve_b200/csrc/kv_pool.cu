@@ -28,37 +28,70 @@ namespace rmlx {
 
 
 // ---------------------------------------------------------------------------
-// Append (plain): one thread per 16-byte chunk of a (layer, token, kv, head)
-// row.  Consecutive threads walk a row, then the next head, so both the
-// [token][head][dim] source and the head-contiguous tiles are streamed.
+// Append: a CTA covers one layer (blockIdx.y) and a run of tokens; a (layer,
+// token) pair is cpp = 2 x heads x (chunks per row) work units (K then V,
+// head, chunk), which tile the CTA's threads (AppendShape): a thread takes
+// unit x of token jt, jt + tpc, ... (APP tokens), loads all of them, then
+// stores them.  Index arithmetic is 32-bit and done once per thread; the
+// slot of each token is read once per thread.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) append_rows_kernel(PoolGeo g, int l0, int nl, const uint8_t* __restrict__ k,
+constexpr int APPEND_APP = 4;  // tokens per thread
+
+struct AppendShape {
+  int cpp;    // work units per (layer, token)
+  int tpc;    // tokens side by side in a CTA (cpp <= 256), else 1
+  int iters;  // unit rounds per thread (cpp > 256: ceil(cpp / 256)), else 1
+};
+
+__device__ __forceinline__ void append_unit(const AppendShape& sh, int cpr, int heads, int it, int& x, int& jt,
+                                            int& c, int& h, int& kv) {
+  if (sh.tpc > 1) {
+    jt = threadIdx.x / sh.cpp;
+    x = threadIdx.x - jt * sh.cpp;
+  } else {
+    jt = 0;
+    x = threadIdx.x + it * blockDim.x;
+  }
+  if (jt >= sh.tpc) x = sh.cpp;  // a thread past the last whole pair: no unit
+  c = x % cpr;
+  const int hk = x / cpr;
+  h = hk % heads;
+  kv = hk / heads;
+}
+
+__global__ void __launch_bounds__(256) append_rows_kernel(PoolGeo g, int l0, const uint8_t* __restrict__ k,
                                                           const uint8_t* __restrict__ v, int64_t ls, int64_t ts,
                                                           int64_t hs, const int32_t* __restrict__ slots, int T,
-                                                          int cpr, int32_t* err) {
+                                                          int cpr, AppendShape sh, int32_t* err) {
   pdl_wait();
   pdl_release();
-  const int64_t total = (int64_t)nl * T * 2 * g.heads * cpr;
+  const int l = blockIdx.y;
   const int64_t cap = (int64_t)g.nblocks * g.bs;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    int c = (int)(i % cpr);
-    int64_t r = i / cpr;
-    int h = (int)(r % g.heads);
-    r /= g.heads;
-    int kv = (int)(r & 1);
-    r >>= 1;
-    int t = (int)(r % T);
-    int l = (int)(r / T);
-    int32_t s = __ldg(slots + t);
-    if (s < 0) continue;
-    if (s >= cap) {
-      if (c == 0) atomicOr(err, DEV_ERR_SLOT);
-      continue;
+  for (int it = 0; it < sh.iters; ++it) {
+    int x, jt, c, h, kv;
+    append_unit(sh, cpr, g.heads, it, x, jt, c, h, kv);
+    const int t0 = blockIdx.x * sh.tpc * APPEND_APP + jt;
+    int32_t s[APPEND_APP];
+#pragma unroll
+    for (int j = 0; j < APPEND_APP; ++j) {
+      const int t = t0 + j * sh.tpc;
+      s[j] = (x < sh.cpp && t < T) ? __ldg(slots + t) : -1;
+      if (s[j] >= cap) {
+        if (c == 0) atomicOr(err, DEV_ERR_SLOT);
+        s[j] = -1;
+      }
     }
-    int blk = s / g.bs, off = s % g.bs;
-    const uint8_t* src = (kv ? v : k) + l * ls + t * ts + h * hs + c * 16;
-    uint8_t* dst = g.base + g.tile_off(blk, l0 + l, kv, h) + (int64_t)off * g.row_bytes + c * 16;
-    st_stream(dst, ld_stream(src));
+    const uint8_t* src = (kv ? v : k) + l * ls + h * hs + c * 16;
+    uint4 val[APPEND_APP];
+#pragma unroll
+    for (int j = 0; j < APPEND_APP; ++j)
+      if (s[j] >= 0) val[j] = ld_stream(src + (int64_t)(t0 + j * sh.tpc) * ts);
+#pragma unroll
+    for (int j = 0; j < APPEND_APP; ++j) {
+      if (s[j] < 0) continue;
+      const int blk = s[j] / g.bs, off = s[j] - blk * g.bs;
+      st_stream(g.base + g.tile_off(blk, l0 + l, kv, h) + (int64_t)off * g.row_bytes + c * 16, val[j]);
+    }
   }
 }
 
@@ -209,91 +242,86 @@ __device__ __forceinline__ uint32_t quant_code(float v, float mn, float scale, f
 }
 
 // ---------------------------------------------------------------------------
-// Quantise-on-append: one thread per 8 elements of a row; a group of
-// group_size elements is group_size/8 adjacent lanes (a power of two <= 32,
-// aligned, never crossing a warp), reduced with xor shuffles.
+// Quantise-on-append: one thread per 8 elements of a row, the CTAs laid out
+// as for the plain append (one layer per blockIdx.y, AppendShape), one token
+// per thread at a time; a group of group_size elements is group_size/8
+// adjacent lanes (a power of two <= 32, aligned, never crossing a warp: the
+// work units of a row are consecutive and a CTA's thread count is a multiple
+// of 32), reduced with xor shuffles that every lane of the warp takes part
+// in.
 // ---------------------------------------------------------------------------
 template <int IN_DT, int BITS, bool META_F32>
-__global__ void __launch_bounds__(256) append_quant_kernel(PoolGeo g, int l0, int nl, const uint8_t* __restrict__ k,
+__global__ void __launch_bounds__(256) append_quant_kernel(PoolGeo g, int l0, const uint8_t* __restrict__ k,
                                                            const uint8_t* __restrict__ v, int64_t ls, int64_t ts,
                                                            int64_t hs, const int32_t* __restrict__ slots, int T,
-                                                           int hd, int tpg, int32_t* err) {
+                                                           int hd, int tpg, AppendShape sh, int32_t* err) {
   using E = Elem<IN_DT>;
   pdl_wait();
   pdl_release();
   const int cpr = hd / 8;
-  const int64_t total = (int64_t)nl * T * 2 * g.heads * cpr;
+  const int l = blockIdx.y;
   const int64_t cap = (int64_t)g.nblocks * g.bs;
   const float qmax = (float)((1u << BITS) - 1);
-  const int lane = threadIdx.x & 31;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t wb = blockIdx.x * (int64_t)blockDim.x + (threadIdx.x & ~31); wb < total; wb += stride) {
-    const int64_t i = wb + lane;
-    bool valid = i < total;
-    int c = 0, h = 0, kv = 0, t = 0, l = 0;
-    int32_t s = -1;
-    if (valid) {
-      c = (int)(i % cpr);
-      int64_t r = i / cpr;
-      h = (int)(r % g.heads);
-      r /= g.heads;
-      kv = (int)(r & 1);
-      r >>= 1;
-      t = (int)(r % T);
-      l = (int)(r / T);
-      s = __ldg(slots + t);
+  for (int it = 0; it < sh.iters; ++it) {
+    int x, jt, c, h, kv;
+    append_unit(sh, cpr, g.heads, it, x, jt, c, h, kv);
+    const int t0 = blockIdx.x * sh.tpc * APPEND_APP + jt;
+    const uint8_t* src = (kv ? v : k) + l * ls + h * hs + (int64_t)c * 8 * E::size;
+    for (int j = 0; j < APPEND_APP; ++j) {
+      const int t = t0 + j * sh.tpc;
+      int32_t s = (x < sh.cpp && t < T) ? __ldg(slots + t) : -1;
       if (s >= cap) {
         if (c == 0) atomicOr(err, DEV_ERR_SLOT);
         s = -1;
       }
-      valid = s >= 0;
-    }
-    float f[8];
-    if (valid) {
-      E::load8((kv ? v : k) + l * ls + t * ts + h * hs + (int64_t)c * 8 * E::size, f);
-    } else {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) f[e] = 0.0f;
-    }
-    float mx = -INFINITY, mn = INFINITY;
-#pragma unroll
-    for (int e = 0; e < 8; ++e) mx = fmaxf(mx, f[e]);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) mn = fminf(mn, f[e]);
-    for (int o = 1; o < tpg; o <<= 1) {
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
-    }
-    if (!valid) continue;
-    const float range = __fsub_rn(mx, mn);
-    const float scale = (range == 0.0f) ? 1.0f : __fdiv_rn(range, qmax);
-    const int blk = s / g.bs, off = s % g.bs;
-    uint8_t* tile = g.base + g.tile_off(blk, l0 + l, kv, h);
-    uint8_t* code_row = tile + (int64_t)off * g.row_bytes;
-    if (BITS == 8) {
-      uint32_t lo = 0, hi = 0;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) lo |= quant_code(f[e], mn, scale, qmax) << (8 * e);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) hi |= quant_code(f[4 + e], mn, scale, qmax) << (8 * e);
-      *reinterpret_cast<uint2*>(code_row + c * 8) = make_uint2(lo, hi);
-    } else {
-      uint32_t w = 0;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        uint32_t a = quant_code(f[2 * e], mn, scale, qmax), b = quant_code(f[2 * e + 1], mn, scale, qmax);
-        w |= (a | (b << 4)) << (8 * e);
-      }
-      *reinterpret_cast<uint32_t*>(code_row + c * 4) = w;
-    }
-    if ((c & (tpg - 1)) == 0) {
-      const int q = c / tpg;
-      uint8_t* meta_row = tile + (int64_t)g.bs * g.row_bytes + (int64_t)off * g.meta_row_bytes;
-      if (META_F32) {
-        reinterpret_cast<float*>(meta_row)[2 * q] = scale;
-        reinterpret_cast<float*>(meta_row)[2 * q + 1] = mn;
+      const bool valid = s >= 0;
+      float f[8];
+      if (valid) {
+        E::load8(src + (int64_t)t * ts, f);
       } else {
-        reinterpret_cast<__half2*>(meta_row)[q] = __halves2half2(__float2half_rn(scale), __float2half_rn(mn));
+#pragma unroll
+        for (int e = 0; e < 8; ++e) f[e] = 0.0f;
+      }
+      float mx = -INFINITY, mn = INFINITY;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) mx = fmaxf(mx, f[e]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) mn = fminf(mn, f[e]);
+      for (int o = 1; o < tpg; o <<= 1) {
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+      }
+      if (!valid) continue;
+      const float range = __fsub_rn(mx, mn);
+      const float scale = (range == 0.0f) ? 1.0f : __fdiv_rn(range, qmax);
+      const int blk = s / g.bs, off = s - blk * g.bs;
+      uint8_t* tile = g.base + g.tile_off(blk, l0 + l, kv, h);
+      uint8_t* code_row = tile + (int64_t)off * g.row_bytes;
+      if (BITS == 8) {
+        uint32_t lo = 0, hi = 0;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) lo |= quant_code(f[e], mn, scale, qmax) << (8 * e);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) hi |= quant_code(f[4 + e], mn, scale, qmax) << (8 * e);
+        *reinterpret_cast<uint2*>(code_row + c * 8) = make_uint2(lo, hi);
+      } else {
+        uint32_t w = 0;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          uint32_t a = quant_code(f[2 * e], mn, scale, qmax), b = quant_code(f[2 * e + 1], mn, scale, qmax);
+          w |= (a | (b << 4)) << (8 * e);
+        }
+        *reinterpret_cast<uint32_t*>(code_row + c * 4) = w;
+      }
+      if ((c & (tpg - 1)) == 0) {
+        const int q = c / tpg;
+        uint8_t* meta_row = tile + (int64_t)g.bs * g.row_bytes + (int64_t)off * g.meta_row_bytes;
+        if (META_F32) {
+          reinterpret_cast<float*>(meta_row)[2 * q] = scale;
+          reinterpret_cast<float*>(meta_row)[2 * q + 1] = mn;
+        } else {
+          reinterpret_cast<__half2*>(meta_row)[q] = __halves2half2(__float2half_rn(scale), __float2half_rn(mn));
+        }
       }
     }
   }
@@ -701,8 +729,8 @@ using namespace rmlx;
 namespace {
 
 // Dispatch tables for the templated quantised kernels.
-using AppendQuantFn = void (*)(PoolGeo, int, int, const uint8_t*, const uint8_t*, int64_t, int64_t, int64_t,
-                               const int32_t*, int, int, int, int32_t*);
+using AppendQuantFn = void (*)(PoolGeo, int, const uint8_t*, const uint8_t*, int64_t, int64_t, int64_t,
+                               const int32_t*, int, int, int, AppendShape, int32_t*);
 template <int IN, int BITS, bool MF32>
 AppendQuantFn aq() {
   return append_quant_kernel<IN, BITS, MF32>;
@@ -894,20 +922,32 @@ rmlx_status rmlx_kv_append(rmlx_kv_pool* p, int32_t layer_begin, int32_t num_lay
   PoolGeo g = p->geo();
   const uint8_t* kb = (const uint8_t*)k;
   const uint8_t* vb = (const uint8_t*)v;
+  if (num_layers > 65535) return fail(RMLX_E_BAD_ARG, "more than 65535 layers in one append");
+  // work units per (layer, token): 16-byte chunks (plain) or 8-element
+  // chunks (quantised) of the K and V rows of every head
+  const int cpr = c.quant_bits == 0 ? (int)(p->row_bytes / 16) : c.head_dim / 8;
+  AppendShape sh;
+  sh.cpp = 2 * c.num_kv_heads * cpr;
+  int block;
+  if (sh.cpp <= 256) {
+    sh.tpc = 256 / sh.cpp;
+    sh.iters = 1;
+    block = (sh.tpc * sh.cpp + 31) / 32 * 32;
+  } else {
+    sh.tpc = 1;
+    sh.iters = (sh.cpp + 255) / 256;
+    block = 256;
+  }
+  const dim3 grid((unsigned)((T + sh.tpc * APPEND_APP - 1) / (sh.tpc * APPEND_APP)), (unsigned)num_layers);
   if (c.quant_bits == 0) {
-    const int cpr = (int)(p->row_bytes / 16);
-    const int64_t total = (int64_t)num_layers * T * 2 * c.num_kv_heads * cpr;
-    const int grid = (int)std::min<int64_t>((total + 255) / 256, (int64_t)p->num_sms * 16);
-    cudaError_t e = launch_pdl(append_rows_kernel, dim3(grid), dim3(256), 0, st, g, layer_begin, num_layers, kb, vb, ls,
-                               ts, hs, slots, T, cpr, p->err);
+    cudaError_t e = launch_pdl(append_rows_kernel, grid, dim3(block), 0, st, g, layer_begin, kb, vb, ls, ts, hs, slots,
+                               T, cpr, sh, p->err);
     if (e != cudaSuccess) return cuda_check(e, "append launch");
   } else {
     const int tpg = c.group_size / 8;
-    const int64_t total = (int64_t)num_layers * T * 2 * c.num_kv_heads * (c.head_dim / 8);
-    const int grid = (int)std::min<int64_t>((total + 255) / 256, (int64_t)p->num_sms * 16);
     AppendQuantFn fn = pick_append_quant(c.dtype, c.quant_bits, c.meta_dtype == RMLX_F32);
-    cudaError_t e = launch_pdl(fn, dim3(grid), dim3(256), 0, st, g, layer_begin, num_layers, kb, vb, ls, ts, hs, slots,
-                               T, c.head_dim, tpg, p->err);
+    cudaError_t e = launch_pdl(fn, grid, dim3(block), 0, st, g, layer_begin, kb, vb, ls, ts, hs, slots, T,
+                               c.head_dim, tpg, sh, p->err);
     if (e != cudaSuccess) return cuda_check(e, "append launch");
   }
   return cuda_check(cudaGetLastError(), "append launch");
