@@ -1015,16 +1015,23 @@ def main():
     g_bytes = float(np.mean(gather_bytes))
     g_ms = float(np.mean(gather_ms))
 
-    # The append alone: the K timed steps' appends again, back to back, CUDA
-    # events around them (each launch overlaps the previous one's tail, as
-    # in the step); average launch = span / K.
+    # The append alone: the K timed steps' appends again, back to back,
+    # captured once in a CUDA graph and replayed between CUDA events (issued
+    # one by one from Python, each launch would wait for the host: the
+    # append's device time is a few microseconds); average launch = span / K.
     a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    g_app = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_app, capture_error_mode="relaxed"):
+        cap = torch.cuda.current_stream().cuda_stream
+        for i in range(K):
+            rc |= lib.rmlx_kv_append(h, 0, L, new_k[W + i].data_ptr(), new_v[W + i].data_ptr(), ls, ts, hs,
+                                     slots_d[W + i].data_ptr(), B, cap)
+    torch.cuda.synchronize()
     a0.record(stream)
-    for i in range(K):
-        rc |= lib.rmlx_kv_append(h, 0, L, new_k[W + i].data_ptr(), new_v[W + i].data_ptr(), ls, ts, hs,
-                                 slots_d[W + i].data_ptr(), B, sp)
+    g_app.replay()
     a1.record(stream)
     torch.cuda.synchronize()
+    del g_app
     if rc or pool.check() != 0:
         raise SystemExit("launch or device-side validation error in the append timing")
     append_ms = a0.elapsed_time(a1) / K
@@ -1207,7 +1214,8 @@ def main():
                        "algorithmic_bytes_per_launch": int(append_bytes), "launch_ms": round(append_ms, 4),
                        "achieved": round(append_bytes / (append_ms * 1e-3) / 1e9, 1),
                        "frac": round(append_bytes / (append_ms * 1e-3) / 1e9 / peak, 4),
-                       "what": "the timed steps' appends again, back to back (all layers, one launch per step)"},
+                       "what": "the timed steps' appends again, back to back from one CUDA graph (all layers, "
+                               "one launch per step)"},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": 4, "ms_per_step": round(e2e_s / K * 1e3, 4)},
             "gpu_launches": K * (1 + (1 if multi else (2 if G else 1) * L)),
