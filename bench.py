@@ -917,17 +917,12 @@ def main():
     layer_elems = int(lens_steps[-1].sum()) * H * D  # each layer's gathered K (or V), elements
     ls = B * H * D
 
-    def launch_step(s, ev_pair=None, sp=sp, gathers_only=False):
-        """The append, then the gather of every layer.  ev_pair brackets the
-        step's gathers (not each launch: events between launches would stop
-        consecutive kernels from overlapping their launch with the tail of
-        the previous one)."""
+    def launch_step(s, sp=sp, gathers_only=False):
+        """The append, then the gather of every layer (or its attention)."""
         rc = 0
         if not gathers_only:
             rc = lib.rmlx_kv_append(h, 0, L, new_k[s].data_ptr(), new_v[s].data_ptr(), ls, ts, hs,
                                     slots_d[s].data_ptr(), B, sp)
-        if ev_pair is not None:
-            ev_pair[0].record(stream)
         if multi:
             rc |= lib.rmlx_kv_gather_layers(h, 0, L, bt_d.data_ptr(), bt.shape[1], lens_d[s].data_ptr(), B,
                                             out_k.data_ptr(), out_v.data_ptr(), layer_elems, sp)
@@ -939,8 +934,6 @@ def main():
             else:
                 rc |= lib.rmlx_kv_gather(h, layer, bt_d.data_ptr(), bt.shape[1], lens_d[s].data_ptr(), B,
                                          out_k.data_ptr(), out_v.data_ptr(), sp)
-        if ev_pair is not None:
-            ev_pair[1].record(stream)
         return rc
 
     def barrier():
@@ -962,7 +955,7 @@ def main():
 
     clocks = Clocks(dev)
     clocks.start()
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))]
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if w.graph:
         # Latency-bound steps: issuing them from Python leaves the GPU idle
@@ -985,21 +978,24 @@ def main():
         g_steps.replay()
     else:
         for i in range(K):
-            rc |= launch_step(W + i, ev[i])
+            rc |= launch_step(W + i)
     e1.record(stream)
     torch.cuda.synchronize()
     barrier()
     elapsed_ms = max_over_ranks(e0.elapsed_time(e1))
+    # The gather (or attention) launch time: the K steps' gathers alone, back
+    # to back after the timed region, events around them all (events between
+    # launches inside the timed steps would stop consecutive kernels from
+    # overlapping their launch with the previous one's tail).
+    ev[0][0].record(stream)
     if w.graph:
-        # the gather launch time: the K steps' gathers alone, replayed after them
-        ev[0][0].record(stream)
         g_gathers.replay()
-        ev[0][1].record(stream)
-        torch.cuda.synchronize()
-        gather_ms = [ev[0][0].elapsed_time(ev[0][1]) / (K * (1 if multi else L))]
     else:
-        # average gather launch = a step's gather span / its launches
-        gather_ms = [ev[i][0].elapsed_time(ev[i][1]) / (1 if multi else L) for i in range(K)]
+        for i in range(K):
+            rc |= launch_step(W + i, gathers_only=True)
+    ev[0][1].record(stream)
+    torch.cuda.synchronize()
+    gather_ms = [ev[0][0].elapsed_time(ev[0][1]) / (K * (1 if multi else L))]
     if rc or pool.check() != 0:
         raise SystemExit("launch or device-side validation error in the timed region")
 
