@@ -1003,11 +1003,14 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
       };
 
       // S^T = K Q^T, folded into sacc at the end of each group
-      float sacc[NH][4], sgp[NH][4];
+      // a group's products; 4-bit: even k-steps in sgp, odd in sgq (two
+      // shorter MMA chains; measured 86.6 against 88.5 us per layer, while
+      // 8-bit pools measured no gain)
+      float sacc[NH][4], sgp[NH][4], sgq[NH][4];
 #pragma unroll
       for (int n = 0; n < NH; ++n)
 #pragma unroll
-        for (int k = 0; k < 4; ++k) sacc[n][k] = sgp[n][k] = 0.0f;
+        for (int k = 0; k < 4; ++k) sacc[n][k] = sgp[n][k] = sgq[n][k] = 0.0f;
 #pragma unroll
       for (int sc2 = 0; sc2 < NSEG; sc2 += 2) {
         uint32_t wv[4];  // tokens 0-7 | 8-15 of column sc2, then of column sc2 + 1
@@ -1037,7 +1040,8 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
           for (int u = 0; u < MPS; ++u) {
             const int kk = (sc2 + half) * MPS + u;
 #pragma unroll
-            for (int n = 0; n < NH; ++n) mma16816<RMLX_F16>(sgp[n], a[u], qb[n][kk][0], qb[n][kk][1]);
+            for (int n = 0; n < NH; ++n)
+              mma16816<RMLX_F16>((BITS == 4 && (kk & 1)) ? sgq[n] : sgp[n], a[u], qb[n][kk][0], qb[n][kk][1]);
             if (((kk + 1) * 16) % GS == 0) {  // the group ends with this k-step
               const int gk = kk * 16 / GS;
               float s0, z0, s1, z1;
@@ -1049,6 +1053,10 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
               for (int n = 0; n < NH; ++n) {
                 const float* qx = qsx[n][gk];
                 const float* qy = qsy[n][gk];
+                if (BITS == 4) {
+#pragma unroll
+                  for (int k = 0; k < 4; ++k) sgp[n][k] += sgq[n][k];
+                }
                 float t[4] = {fmaf(s0, sgp[n][0], zx0 * qx[0]), fmaf(s0, sgp[n][1], zx0 * qx[1]),
                               fmaf(s1, sgp[n][2], zx1 * qx[0]), fmaf(s1, sgp[n][3], zx1 * qx[1])};
                 if (BITS == 4) {
@@ -1060,7 +1068,7 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, MINB)
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
                   sacc[n][k] += t[k];
-                  sgp[n][k] = 0.0f;
+                  sgp[n][k] = sgq[n][k] = 0.0f;
                 }
               }
             }
