@@ -629,7 +629,7 @@ class Clocks:
     """nvidia-smi sampling of SM clocks and throttle reasons during timing."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap,clocks.mem")
 
     def __init__(self, device):
         self.device = device
@@ -656,7 +656,7 @@ class Clocks:
         except subprocess.TimeoutExpired:
             self.proc.kill()
         self.f.close()
-        sm, mx, reasons = [], 0.0, set()
+        sm, mem, mx, reasons = [], [], 0.0, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for ln in open(self.path):
             p = [x.strip() for x in ln.split(",")]
@@ -670,12 +670,20 @@ class Clocks:
             for n, v in zip(names, p[5:9]):
                 if v.lower().startswith("active"):
                     reasons.add(n)
+            if len(p) > 9:
+                try:
+                    mem.append(float(p[9]))
+                except ValueError:
+                    pass
         os.unlink(self.path)
         self.proc = None
         if not sm:
             return None
-        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        out = {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        if mem:
+            out["mem_mhz"] = float(np.median(mem))
+            out["mem_mhz_min"] = float(min(mem))
+        return out
 
 
 def cpu_sample(w, steps, warm, threads, lens0, bt, slots, num_blocks, seqs=None):
