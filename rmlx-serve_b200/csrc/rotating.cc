@@ -30,6 +30,7 @@ struct rmlx_rotating {
   int64_t bs, max_size, keep;
   int64_t offset = 0, written = 0;
   std::vector<int32_t> table;
+  std::vector<int32_t> last;  // append_slots: the token that last took each ring position (-1: none)
 
   int64_t rotating() const { return max_size - keep; }
   int64_t seq_len() const { return written < max_size ? written : max_size; }
@@ -98,15 +99,31 @@ rmlx_status rmlx_rotating_append_slots(rmlx_rotating* r, int32_t n, int32_t* slo
     }
   }
   // A position written twice within the call keeps the later token; the
-  // earlier one's slot is -1, which rmlx_kv_append skips.
-  std::vector<int32_t> last((size_t)r->max_size, -1);
+  // earlier one's slot is -1, which rmlx_kv_append skips.  A call can revisit
+  // a position only when it has more tokens than the ring rotates through,
+  // or when a trim of a rotated ring left written < max_size with a nonzero
+  // offset (the linear fill then runs into the rotating positions).
+  const bool revisit =
+      n > 1 && ((int64_t)n > r->rotating() || (r->written < r->max_size && r->offset != 0));
+  if (revisit && r->last.size() != (size_t)r->max_size) r->last.assign((size_t)r->max_size, -1);
+  const int64_t w0 = r->written, off0 = r->offset;
   for (int32_t t = 0; t < n; ++t) {
     const int64_t pos = r->next_pos(r->written, r->offset);
     slots[t] = r->slot(pos);
-    if (last[pos] >= 0) slots[last[pos]] = -1;
-    last[pos] = t;
+    if (revisit) {
+      if (r->last[pos] >= 0) slots[r->last[pos]] = -1;
+      r->last[pos] = t;
+    }
     if (r->written >= r->max_size) r->offset = (r->offset + 1) % r->rotating();
     ++r->written;
+  }
+  if (revisit) {  // leave the scratch all -1 for the next call
+    int64_t w = w0, off = off0;
+    for (int32_t t = 0; t < n; ++t) {
+      r->last[r->next_pos(w, off)] = -1;
+      if (w >= r->max_size) off = (off + 1) % r->rotating();
+      ++w;
+    }
   }
   return RMLX_OK;
 }
