@@ -55,6 +55,12 @@ def share_nccl_id(group=None) -> bytes:
 _EPOCH = {}
 
 
+def reset_plan_counts() -> None:
+    """Forget this process's exchange counts (for a new job sharing the
+    process with a new store and new peers)."""
+    _EPOCH.clear()
+
+
 def _default_store():
     from torch.distributed import distributed_c10d
     return distributed_c10d._get_default_store()
@@ -91,7 +97,11 @@ def exchange_migration_plan(mgr, send_ids: List[int], peer: int, group=None, *, 
     blocks coming to it (nothing is allocated then).
 
     Both ranks of a pair call this the same number of times in the same
-    order; the n-th call of each is matched with the n-th call of the other.
+    order; the n-th call of each is matched with the n-th call of the other
+    (a per-process count of the pair's exchanges).  After an exchange has
+    failed the two counts may disagree: treat the peer as gone, and pair a
+    replacement process with this one only through a fresh store and a
+    fresh process (or ``reset_plan_counts``).
     """
     import time
     import torch.distributed as dist
