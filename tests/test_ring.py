@@ -128,3 +128,27 @@ def test_ring_closes_before_its_manager():
     mgr = rb._mgr
     rb.close()
     assert mgr.num_free_blocks() == 8
+
+
+def test_ring_c_abi_argument_checks():
+    """The C ABI's own checks: a block size other than the manager's, NULL
+    outputs, negative counts, and a trim past what is trimmable (the
+    reference's panic) leave the ring as it was."""
+    import ctypes as C
+    from rmlx_kv import _lib
+    lib = _lib.lib
+    m = rmlx_kv.PagedCacheManager(4, 16)
+    h = _lib.vp()
+    assert lib.rmlx_rotating_new(m._h, 8, 10, 2, C.byref(h)) == _lib.RMLX_E_BAD_ARG  # manager uses 4
+    assert lib.rmlx_rotating_new(m._h, 4, 10, -1, C.byref(h)) == _lib.RMLX_E_BAD_ARG
+    rb = RotatingBlocks(m, 4, 10, 2)
+    assert lib.rmlx_rotating_append_slots(rb._h, -1, None) == _lib.RMLX_E_BAD_ARG
+    assert lib.rmlx_rotating_append_slots(rb._h, 3, None) == _lib.RMLX_E_BAD_ARG
+    assert lib.rmlx_rotating_append_slots(rb._h, 0, None) == _lib.RMLX_OK
+    rb.append_slots(5)
+    n = C.c_int32()
+    assert lib.rmlx_rotating_trim(rb._h, 4, None, None, 0, C.byref(n)) == _lib.RMLX_E_RANGE
+    assert lib.rmlx_rotating_trim(rb._h, -1, None, None, 0, C.byref(n)) == _lib.RMLX_E_BAD_ARG
+    assert lib.rmlx_rotating_blocks(rb._h, None, 0, C.byref(n)) == _lib.RMLX_OK and n.value == 2
+    assert rb.seq_len() == 5 and rb.written == 5 and rb.ring_offset() == -1
+    assert lib.rmlx_rotating_max_size(rb._h) == 10 and lib.rmlx_rotating_keep(rb._h) == 2
